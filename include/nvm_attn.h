@@ -1,0 +1,201 @@
+/*
+ * nvm_attn.h -- C ABI of libnvm_attn.so, the B200 (sm_100a) attention hot path of
+ * nano-vllm-metal: paged-attention decode / multi-query, dense flash attention,
+ * the paged KV scatter-write (with int8 quantise-on-write) and device-side page
+ * allocation for a batch of appends.
+ *
+ * Conventions shared by every entry point
+ *   - All tensor arguments are raw DEVICE pointers to row-major contiguous memory
+ *     (strides are given explicitly where an argument may be a strided view).
+ *   - Sizes are int64_t element counts.  Element types are `nvm_dtype` codes.
+ *   - `stream` is a cudaStream_t passed as void*; every call is stream-ordered and
+ *     never synchronises the device.  NULL means the legacy default stream.
+ *   - Return value: NVM_OK (0) or a negative nvm_status.  No C++ exception crosses
+ *     the ABI.  nvm_last_error() returns the message of the last failing call on
+ *     the calling thread; messages start with the reference operator's name
+ *     ("paged_attention: ...", "flash_attention: ...") so a Python wrapper can
+ *     re-raise them verbatim.
+ *   - The library holds no mutable global state apart from a per-device error word
+ *     written by kernels whose bounded waits expire (nvm_device_error()).
+ *
+ * Reference interfaces replaced (paths inside PepperoniBlvd/nano-vllm-metal):
+ *   src/nano_vllm_metal/metal/bindings.cpp:34-82           (nanobind _ext module)
+ *   src/nano_vllm_metal/metal/src/kernels.h:37-75          (operator declarations)
+ *   src/nano_vllm_metal/metal/src/paged_attention.cpp:19-120, 413-642
+ *   src/nano_vllm_metal/metal/src/flash_attention.cpp:17-61, 251-352
+ *   src/nano_vllm_metal/cache/paged.py:152-195             (page write + int8 quantiser)
+ *   src/nano_vllm_metal/cache/paged.py:60-70, 424-459      (page allocation on append)
+ */
+#ifndef NVM_ATTN_H_
+#define NVM_ATTN_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Element type codes. */
+typedef enum nvm_dtype {
+  NVM_F32 = 0,
+  NVM_F16 = 1,
+  NVM_BF16 = 2,
+  NVM_I8 = 3,
+  NVM_I32 = 4,
+  NVM_I64 = 5
+} nvm_dtype;
+
+/* Status codes (0 = success). */
+typedef enum nvm_status {
+  NVM_OK = 0,
+  NVM_ERR_INVALID_ARGUMENT = -1, /* bad shape / dtype / pointer combination      */
+  NVM_ERR_UNSUPPORTED = -2,      /* valid request this build cannot serve        */
+  NVM_ERR_WORKSPACE = -3,        /* workspace missing or smaller than required   */
+  NVM_ERR_CUDA = -4,             /* a CUDA runtime / driver call failed          */
+  NVM_ERR_DEVICE_TIMEOUT = -5,   /* a kernel's bounded wait expired (see below)  */
+  NVM_ERR_OUT_OF_PAGES = -6      /* page allocation exceeded the pool capacity   */
+} nvm_status;
+
+/* Human-readable name of a status code (static string). */
+const char* nvm_status_string(int status);
+
+/* Detailed message of the last failing call on this thread ("" if none). */
+const char* nvm_last_error(void);
+
+/* Library version string, e.g. "nvm_attn 0.1 sm_100a". */
+const char* nvm_version(void);
+
+/*
+ * Device error word.  Kernels that spin on an mbarrier give every wait an
+ * iteration/time limit; when one expires the kernel records a nonzero code here,
+ * drains its own in-flight copies (bounded) and returns, leaving the context
+ * usable.  nvm_device_error() synchronises `stream`, reads the word of the current
+ * device, optionally clears it, and returns it (0 = no error).
+ */
+int nvm_device_error(void* stream, int clear);
+
+/* ------------------------------------------------------------------------- */
+/* Paged attention (decode, multi-token verify, chunked prefill)              */
+/* ------------------------------------------------------------------------- */
+/*
+ * Replaces: _ext.paged_attention / _ext.paged_attention_int8_decode
+ *   (src/nano_vllm_metal/metal/bindings.cpp:34-66,
+ *    src/nano_vllm_metal/metal/src/paged_attention.cpp:19-120 validation,
+ *    :413-574 and :576-642 GPU dispatch) and the dequantise-then-attend int8 L>1
+ *    path of src/nano_vllm_metal/layers/attention.py:204-215 (done in-kernel here).
+ *
+ * q            [B*Hq, L, D] of q_dtype (F32/F16/BF16), row n = b*Hq + head.
+ * k_pages,
+ * v_pages      [P, Hkv, page_size, D] of kv_dtype (F32/F16/BF16/I8).
+ * k_scales,
+ * v_scales     [P, Hkv, page_size, 1] of scale_dtype (F32/F16/BF16); required iff
+ *              kv_dtype == NVM_I8, else NULL.  value = int8 * scale.
+ * block_table  [B, max_pages] int32 physical page ids; entries < 0 (or >= P) are
+ *              holes whose positions are skipped, as in paged_attention.cpp:216-222.
+ * context_lens [B] int32; context_len <= 0 gives a zero output row block.
+ * out          [B*Hq, L, D] of out_dtype (F32/F16/BF16); the reference returns F32.
+ * scale        softmax scale applied to q.k.
+ * is_causal    row l of L may see key positions <= l + context_len - L.
+ * workspace    device scratch of at least nvm_paged_attention_workspace_size(...)
+ *              bytes, ZERO-FILLED before its first use; every successful call
+ *              leaves it zero-filled again.  May be NULL if that size is 0.
+ *              Calls that share one workspace must not overlap on the GPU.
+ */
+int nvm_paged_attention(const void* q, int q_dtype, const void* k_pages, const void* v_pages,
+                        int kv_dtype, const void* k_scales, const void* v_scales, int scale_dtype,
+                        const int32_t* block_table, const int32_t* context_lens, void* out,
+                        int out_dtype, int64_t B, int64_t Hq, int64_t Hkv, int64_t L, int64_t D,
+                        int64_t P, int64_t page_size, int64_t max_pages, float scale,
+                        int is_causal, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Workspace bytes nvm_paged_attention needs for these sizes (0 if none). */
+size_t nvm_paged_attention_workspace_size(int64_t B, int64_t Hq, int64_t Hkv, int64_t L,
+                                          int64_t D, int64_t page_size, int64_t max_pages,
+                                          int kv_dtype);
+
+/* ------------------------------------------------------------------------- */
+/* Dense flash attention (prefill)                                            */
+/* ------------------------------------------------------------------------- */
+/*
+ * Replaces: _ext.flash_attention (src/nano_vllm_metal/metal/bindings.cpp:68-82,
+ *   src/nano_vllm_metal/metal/src/flash_attention.cpp:17-61 validation, :251-352
+ *   dispatch) and the MLX fast SDPA call of the initial-prefill branch
+ *   (src/nano_vllm_metal/models/qwen3.py:137-144).
+ *
+ * q            [B*Hq, L, D], k/v [B*Hkv, S, D], all of `dtype` (F32/F16/BF16).
+ * mask         optional additive F32 mask read as mask[n*ms_n + l*ms_l + s*ms_s]
+ *              (strides in elements, 0 broadcasts), or NULL.  With is_causal the
+ *              rows see keys s <= l + S - L (flash_attention.cpp:132-139) and the
+ *              mask, when given, is added on the visible keys only for tiles that
+ *              are not fully visible -- exactly the reference's block skip.
+ * out          [B*Hq, L, D] of out_dtype.
+ */
+int nvm_flash_attention(const void* q, const void* k, const void* v, int dtype, const float* mask,
+                        int64_t mask_stride_n, int64_t mask_stride_l, int64_t mask_stride_s,
+                        void* out, int out_dtype, int64_t B, int64_t Hq, int64_t Hkv, int64_t L,
+                        int64_t S, int64_t D, float scale, int is_causal, void* stream);
+
+/* ------------------------------------------------------------------------- */
+/* Paged KV scatter-write (+ int8 quantise-on-write)                          */
+/* ------------------------------------------------------------------------- */
+/*
+ * Replaces: TinyKvPagedPool.write_page_slice / _quantize_page_slice
+ *   (src/nano_vllm_metal/cache/paged.py:152-195) as driven by
+ *   TinyKvPagedCache._append_chunk (paged.py:424-459) and
+ *   BatchingKvCache.update_and_fetch_paged (src/nano_vllm_metal/cache/kv_cache.py:134-151).
+ *
+ * k, v         token t, head h element d at k[t*stride_t + h*stride_h + d]
+ *              (element strides; d is contiguous), of in_dtype (F32/F16/BF16).
+ * slot_mapping [T] int64: slot = page_id*page_size + offset, or < 0 to skip.
+ * k_pages,
+ * v_pages      [P, Hkv, page_size, D] of kv_dtype.  kv_dtype == in_dtype copies the
+ *              bits; kv_dtype == NVM_I8 quantises each (token, head) row:
+ *                amax = max|x| (fp32); s = amax > 0 ? amax/127 : 1;
+ *                q = clip(round_half_even(x / s), -127, 127);
+ *              and stores s rounded to scale_dtype in k_scales / v_scales
+ *              [P, Hkv, page_size, 1] (paged.py:153-158).
+ * Pages are mutated in place (the reference's buffer-donating slice-assign).
+ */
+int nvm_reshape_and_cache(const void* k, const void* v, int in_dtype, int64_t stride_t,
+                          int64_t stride_h, void* k_pages, void* v_pages, int kv_dtype,
+                          void* k_scales, void* v_scales, int scale_dtype,
+                          const int64_t* slot_mapping, int64_t T, int64_t Hkv, int64_t D,
+                          int64_t P, int64_t page_size, void* stream);
+
+/* ------------------------------------------------------------------------- */
+/* Device-side page allocation for one batched append                         */
+/* ------------------------------------------------------------------------- */
+/*
+ * Replaces, for a whole batch at once and on the device: the per-request loop of
+ * BatchingKvCache.update_and_fetch_paged (src/nano_vllm_metal/cache/kv_cache.py:134-173)
+ * over TinyKvPagedCache._append_chunk (src/nano_vllm_metal/cache/paged.py:424-459)
+ * and TinyKvPagedPool.allocate_page (paged.py:60-70).
+ *
+ * Request b appends new_tokens[b] >= 0 tokens (0 for an idle slot) after its
+ * context_lens[b] existing tokens.  The tail page is filled first, then fresh
+ * pages are popped, in request order, from the free stack (LIFO: the page taken
+ * next is free_stack[*free_top - 1]); when the stack is empty fresh ids
+ * *num_pages, *num_pages+1, ... are minted -- the same ids, in the same order, as
+ * the reference's sequential allocate_page calls.  On success:
+ *   block_table[b, :] gains the new page ids (row width max_pages),
+ *   page_refcount[id] = 1 for each new page,
+ *   slot_mapping[tok_offsets[b] + i] = slot of new token i of request b
+ *     (tok_offsets = exclusive prefix sum of new_tokens, computed in-kernel),
+ *   context_lens[b] += new_tokens[b], *free_top and *num_pages are updated.
+ * capacity bounds minted ids; exceeding it, a block-table row, or the
+ * slot_capacity entries of slot_mapping sets *status = NVM_ERR_OUT_OF_PAGES
+ * (checked on the device before anything is written; nothing is written then).
+ * Single CTA; B <= 4096.  The device ints are int32.
+ */
+int nvm_paged_append(int32_t* block_table, int32_t* context_lens, const int32_t* new_tokens,
+                     int32_t* free_stack, int32_t* free_top, int32_t* num_pages,
+                     int32_t* page_refcount, int64_t* slot_mapping, int64_t slot_capacity,
+                     int32_t* status, int64_t B, int64_t max_pages, int64_t page_size,
+                     int64_t capacity, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NVM_ATTN_H_ */

@@ -1,0 +1,642 @@
+// paged_mma.cu -- tensor-core paged attention for decode, multi-token verify and
+// chunked prefill (and dense attention viewed as one page per sequence).
+//
+// Replaces the reference's Metal kernels paged_attention_decode_split_kv
+// (paged_attention.metal:276-408), paged_attention_kv (:6-128) and
+// paged_attention_int8_decode_kv (:417-525), with the dispatch of
+// paged_attention.cpp:413-642.  Same results, different decomposition:
+//
+//  * One CTA owns one (sequence b, kv head h, row block, key chunk).  The rows are
+//    the g*L query rows that share kv head h (g = Hq/Hkv q heads x L tokens), packed
+//    into 16-row m-tiles, so every K/V byte is read from HBM once per kv head instead
+//    of once per q head as in the reference (grid = B*Hq there).
+//  * Keys are processed in 16-token tiles.  A producer warp streams each tile's K and
+//    V rows ([16][D] contiguous inside one page) with TMA tensor loads (128-byte
+//    swizzle, no multicast) into an NSTAGE-deep shared-memory ring guarded by
+//    mbarriers; page ids come from the block table, holes are skipped.
+//  * Consumer warps run the FA2-style online softmax on mma.sync m16n8k16 (fp32
+//    accumulate): S = Q K^T from ldmatrix'd K, P kept in registers as the A operand
+//    of O += P V with ldmatrix.trans'd V.  int8 pages are converted to f16 in
+//    registers (exact), the per-token key scale multiplies S and the value scale
+//    multiplies V, i.e. dequantisation happens in-kernel for every L.
+//  * Split-K: long contexts are cut into chunks of `chunk_tiles` tiles handled by
+//    separate CTAs; each writes (O, m, l) to the workspace and the last CTA of the
+//    unit (atomic ticket) merges them with log-sum-exp weights and resets the ticket.
+//  * Every mbarrier wait is bounded (nvm::mbar_wait); on expiry the kernel records an
+//    error code, the producer drains what it issued, and the CTA returns.
+#include <type_traits>
+
+#include <cstdio>
+#include <cstdlib>
+#include <mutex>
+
+#include "nvm_common.cuh"
+#include "nvm_internal.h"
+
+namespace nvm {
+namespace {
+
+constexpr int kMaxChunkTiles = 256;
+
+struct MmaParams {
+  const void* q;
+  void* out;
+  const int32_t* block_table;
+  const int32_t* context_lens;
+  float* part_o;      // [units][n_chunks][rows_real][D]
+  float2* part_ml;    // [units][n_chunks][rows_real]
+  int* counters;      // [units]
+  int* err;
+  int q_dtype, out_dtype;
+  int64_t B, Hq, Hkv, L, P, ps, mp, dense_ctx;
+  int64_t g, M;       // q heads per kv head, rows per (b, h)
+  int64_t n_rb, rows_real, ct, n_chunks;
+  float scale_log2;   // softmax scale * log2(e)
+  int causal;
+};
+
+template <typename KvT, int D, int NWM, int NWK>
+struct Cfg {
+  static constexpr bool kI8 = std::is_same<KvT, int8_t>::value;
+  using MmaT = typename std::conditional<kI8, __half, KvT>::type;
+  static constexpr int kCons = NWM * NWK;
+  static constexpr int kThreads = (kCons + 1) * 32;
+  static constexpr int kRB = 16 * NWM;
+  static constexpr int kTileBytes = 16 * D * (int)sizeof(KvT);
+  static constexpr int kScaleBytes = kI8 ? 64 : 0;
+  static constexpr int kStageBytes = ((2 * kTileBytes + kScaleBytes + 1023) / 1024) * 1024;
+  static constexpr int kStages = kI8 ? 12 : 8;
+  static constexpr int kBoxElems = 128 / (int)sizeof(KvT);  // 128-byte inner box (swizzle span)
+  static constexpr int kBoxes = D / kBoxElems;
+  static constexpr int kEpiBytes = NWK * kRB * D * 4 + 2 * NWK * kRB * 4;
+  static constexpr int kRingBytes = kStages * kStageBytes;
+  static constexpr int kMainBytes = kRingBytes > kEpiBytes ? kRingBytes : kEpiBytes;
+  static constexpr int kSmemBytes = 1024 + kMainBytes + kStages * 16 + kStages * 4 + kMaxChunkTiles * 4 + 16;
+  static_assert(kStages % NWK == 0, "stage ring must be a multiple of the k-split");
+  static_assert(D % 64 == 0, "head dim must be 64 or 128");
+  static_assert(!kI8 || D == 128, "int8 path needs D == 128");
+};
+
+// Address of 16-byte chunk `q` of token row `tok` inside a TMA tile written with
+// 128-byte swizzle: boxes of 128 bytes x 16 rows, 2048 bytes each, chunk index XOR row.
+__device__ __forceinline__ uint32_t swz(uint32_t tile, int tok, int q) {
+  return tile + (uint32_t)((q >> 3) * 2048 + tok * 128 + (((q & 7) ^ (tok & 7)) << 4));
+}
+
+template <typename KvT, typename ScaleT, int D, int NWM, int NWK>
+__global__ void __launch_bounds__(Cfg<KvT, D, NWM, NWK>::kThreads)
+    paged_mma_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                     const __grid_constant__ CUtensorMap tm_ks, const __grid_constant__ CUtensorMap tm_vs,
+                     const MmaParams p) {
+  using C = Cfg<KvT, D, NWM, NWK>;
+  using MmaT = typename C::MmaT;
+  constexpr int NS = C::kStages;
+  constexpr int NKS = D / 16;  // k-steps of Q K^T
+  constexpr int NDT = D / 8;   // n8 tiles of the output
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kMainBytes);
+  uint64_t* empty = full + NS;
+  int* stage_valid = reinterpret_cast<int*>(empty + NS);
+  int* tile_pid = stage_valid + NS;
+  int* s_flag = tile_pid + kMaxChunkTiles;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t unit = blockIdx.x;
+  const int64_t rb = unit % p.n_rb;
+  const int64_t bh = unit / p.n_rb;
+  const int64_t h = bh % p.Hkv, b = bh / p.Hkv;
+  const int64_t c = blockIdx.y;
+
+  const int64_t ctx = p.context_lens ? (int64_t)p.context_lens[b] : p.dense_ctx;
+  const int64_t cap = p.mp * p.ps;
+  const int64_t ctx_limit = ctx < cap ? ctx : cap;
+  const int64_t row0 = rb * C::kRB;
+  const int64_t rows_here = (p.M - row0) < C::kRB ? (p.M - row0) : C::kRB;
+  int64_t need_keys = ctx_limit;
+  if (p.causal) {
+    const bool spans = rows_here >= p.L || (row0 % p.L) + rows_here > p.L;
+    const int64_t lmax = spans ? p.L - 1 : (row0 + rows_here - 1) % p.L;
+    const int64_t lim = lmax + ctx - p.L + 1;
+    if (lim < need_keys) need_keys = lim;
+  }
+  if (ctx <= 0 || need_keys < 0) need_keys = 0;
+  const int64_t n_tiles = (need_keys + 15) / 16;
+  const int64_t n_chunks = n_tiles > 0 ? (n_tiles + p.ct - 1) / p.ct : 1;
+  if (c >= n_chunks) return;
+  const int64_t t_begin = c * p.ct;
+  int64_t n_left = n_tiles - t_begin;
+  if (n_left > p.ct) n_left = p.ct;
+  const int n_my = n_left > 0 ? (int)n_left : 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], NWM);
+    }
+    fence_mbar_init();
+  }
+  if (warp == C::kCons) {
+    for (int i = lane; i < n_my; i += 32) {
+      const int64_t tok0 = (t_begin + i) * 16;
+      const int64_t pidx = tok0 / p.ps;
+      const int64_t pid = p.block_table ? (int64_t)p.block_table[b * p.mp + pidx] : b;
+      tile_pid[i] = (pid >= 0 && pid < p.P) ? (int)pid : -1;
+    }
+  }
+  __syncthreads();
+
+  // ------------------------------------------------------------------ producer
+  if (warp == C::kCons) {
+    if (lane == 0) {
+      prefetch_tmap(&tm_k);
+      prefetch_tmap(&tm_v);
+      if (C::kI8) {
+        prefetch_tmap(&tm_ks);
+        prefetch_tmap(&tm_vs);
+      }
+      int issued = 0;
+      for (int i = 0; i < n_my; ++i) {
+        const int s = i % NS;
+        if (i >= NS && !mbar_wait(&empty[s], ((i / NS) & 1) ^ 1)) {
+          record_error(p.err, kDevErrEmptyWait);
+          break;
+        }
+        const int pid = tile_pid[i];
+        stage_valid[s] = pid >= 0 ? 1 : 0;
+        if (pid >= 0) {
+          const int slot0 = (int)(((t_begin + i) * 16) % p.ps);
+          uint8_t* st = smem + s * C::kStageBytes;
+          mbar_arrive_expect_tx(&full[s], 2 * C::kTileBytes + C::kScaleBytes);
+#pragma unroll
+          for (int hb = 0; hb < C::kBoxes; ++hb) {
+            tma_load_4d(st + hb * 2048, &tm_k, hb * C::kBoxElems, slot0, (int)h, pid, &full[s]);
+            tma_load_4d(st + C::kTileBytes + hb * 2048, &tm_v, hb * C::kBoxElems, slot0, (int)h, pid, &full[s]);
+          }
+          if (C::kI8) {
+            tma_load_3d(st + 2 * C::kTileBytes, &tm_ks, slot0, (int)h, pid, &full[s]);
+            tma_load_3d(st + 2 * C::kTileBytes + 32, &tm_vs, slot0, (int)h, pid, &full[s]);
+          }
+        } else {
+          mbar_arrive(&full[s]);
+        }
+        issued = i + 1;
+      }
+      // Drain: the last use of every stage must have landed before the CTA can exit.
+      for (int s = 0; s < NS && s < issued; ++s) {
+        const int last = s + ((issued - 1 - s) / NS) * NS;
+        if (!mbar_wait(&full[s], (last / NS) & 1)) record_error(p.err, kDevErrDrainWait);
+      }
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------------ consumers
+  const int wm = warp % NWM, wk = warp / NWM;
+  const int r = lane >> 2, cq = lane & 3;
+  const int64_t q_row0 = (b * p.Hq + h * p.g) * p.L;  // flat row of (b, h, m = 0)
+  const int64_t mA = row0 + wm * 16 + r, mB = mA + 8;  // this thread's two rows (unit-relative)
+  const bool vA = mA < p.M, vB = mB < p.M;
+
+  uint32_t qa[NKS][4];
+  {
+    const int64_t offA = (q_row0 + mA) * D, offB = (q_row0 + mB) * D;
+#pragma unroll
+    for (int ks = 0; ks < NKS; ++ks) {
+      int d0, d1;  // first d of the low / high k pair of this thread in k-step ks
+      if (C::kI8) {
+        d0 = 32 * cq + 4 * ks;
+        d1 = d0 + 2;
+      } else {
+        d0 = 16 * ks + 2 * cq;
+        d1 = d0 + 8;
+      }
+      float a0 = vA ? load_dyn(p.q, offA + d0, p.q_dtype) : 0.f, a1 = vA ? load_dyn(p.q, offA + d0 + 1, p.q_dtype) : 0.f;
+      float b0 = vB ? load_dyn(p.q, offB + d0, p.q_dtype) : 0.f, b1 = vB ? load_dyn(p.q, offB + d0 + 1, p.q_dtype) : 0.f;
+      float a2 = vA ? load_dyn(p.q, offA + d1, p.q_dtype) : 0.f, a3 = vA ? load_dyn(p.q, offA + d1 + 1, p.q_dtype) : 0.f;
+      float b2 = vB ? load_dyn(p.q, offB + d1, p.q_dtype) : 0.f, b3 = vB ? load_dyn(p.q, offB + d1 + 1, p.q_dtype) : 0.f;
+      qa[ks][0] = pack2<MmaT>(a0, a1);
+      qa[ks][1] = pack2<MmaT>(b0, b1);
+      qa[ks][2] = pack2<MmaT>(a2, a3);
+      qa[ks][3] = pack2<MmaT>(b2, b3);
+    }
+  }
+  // Inclusive last visible key of each row (rows past M never mask anything).
+  const int64_t BIG = INT64_MAX / 4;
+  int64_t limA = BIG, limB = BIG;
+  if (p.causal) {
+    if (vA) limA = (mA % p.L) + ctx - p.L;
+    if (vB) limB = (mB % p.L) + ctx - p.L;
+  }
+  // Keys below `clean` are visible to every real row of this warp: no masking there.
+  int64_t clean = ctx_limit;
+  {
+    int64_t mn = limA < limB ? limA : limB;
+    mn = mn + 1;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int64_t x = __shfl_xor_sync(0xffffffffu, mn, o);
+      mn = x < mn ? x : mn;
+    }
+    if (mn < clean) clean = mn;
+  }
+
+  float mrA = -INFINITY, mrB = -INFINITY, lA = 0.f, lB = 0.f;
+  float o[NDT][4];
+#pragma unroll
+  for (int i = 0; i < NDT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+
+  bool timed_out = false;
+  for (int i = wk; i < n_my; i += NWK) {
+    const int s = i % NS;
+    if (!mbar_wait(&full[s], (i / NS) & 1)) {
+      record_error(p.err, kDevErrFullWait);
+      timed_out = true;
+      break;
+    }
+    if (stage_valid[s]) {
+      const int64_t tok0 = (t_begin + i) * 16;
+      const uint32_t kt = smem_u32(smem + s * C::kStageBytes);
+      const uint32_t vt = kt + C::kTileBytes;
+      float sc[2][4];
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+
+      if constexpr (!C::kI8) {
+        const int mi = lane >> 3;
+        const int ktok = (mi >> 1) * 8 + (lane & 7);
+#pragma unroll
+        for (int ks = 0; ks < NKS; ++ks) {
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4(swz(kt, ktok, 2 * ks + (mi & 1)), b0, b1, b2, b3);
+          mma16816<MmaT>(sc[0], qa[ks], b0, b1);
+          mma16816<MmaT>(sc[1], qa[ks], b2, b3);
+        }
+      } else {
+        uint32_t kw[2][8];
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          const int tok = nt * 8 + r;
+          lds128(swz(kt, tok, 2 * cq), kw[nt][0], kw[nt][1], kw[nt][2], kw[nt][3]);
+          lds128(swz(kt, tok, 2 * cq + 1), kw[nt][4], kw[nt][5], kw[nt][6], kw[nt][7]);
+        }
+#pragma unroll
+        for (int ks = 0; ks < NKS; ++ks) {
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt) {
+            const uint32_t x = kw[nt][ks] ^ 0x80808080u;
+            mma16816<MmaT>(sc[nt], qa[ks], i8pair_to_f16x2(x, 0x4140u), i8pair_to_f16x2(x, 0x4342u));
+          }
+        }
+        const ScaleT* ksp = reinterpret_cast<const ScaleT*>(smem + s * C::kStageBytes + 2 * C::kTileBytes);
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          const float k0 = to_f32(ksp[nt * 8 + 2 * cq]), k1 = to_f32(ksp[nt * 8 + 2 * cq + 1]);
+          sc[nt][0] *= k0;
+          sc[nt][1] *= k1;
+          sc[nt][2] *= k0;
+          sc[nt][3] *= k1;
+        }
+      }
+
+      // scale, mask, online softmax (base 2)
+      const bool need_mask = tok0 + 16 > clean;
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float v = sc[nt][e] * p.scale_log2;
+          if (need_mask) {
+            const int64_t tok = tok0 + nt * 8 + 2 * cq + (e & 1);
+            const int64_t lim = e < 2 ? limA : limB;
+            if (tok >= ctx_limit || tok > lim) v = -INFINITY;
+          }
+          sc[nt][e] = v;
+        }
+      }
+      float mxA = fmaxf(fmaxf(sc[0][0], sc[0][1]), fmaxf(sc[1][0], sc[1][1]));
+      float mxB = fmaxf(fmaxf(sc[0][2], sc[0][3]), fmaxf(sc[1][2], sc[1][3]));
+      mxA = fmaxf(mxA, __shfl_xor_sync(0xffffffffu, mxA, 1));
+      mxA = fmaxf(mxA, __shfl_xor_sync(0xffffffffu, mxA, 2));
+      mxB = fmaxf(mxB, __shfl_xor_sync(0xffffffffu, mxB, 1));
+      mxB = fmaxf(mxB, __shfl_xor_sync(0xffffffffu, mxB, 2));
+      const float mnA = fmaxf(mrA, mxA), mnB = fmaxf(mrB, mxB);
+      const float muA = mnA == -INFINITY ? 0.f : mnA, muB = mnB == -INFINITY ? 0.f : mnB;
+      const float alA = exp2f(mrA - muA), alB = exp2f(mrB - muB);
+      mrA = mnA;
+      mrB = mnB;
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        sc[nt][0] = exp2f(sc[nt][0] - muA);
+        sc[nt][1] = exp2f(sc[nt][1] - muA);
+        sc[nt][2] = exp2f(sc[nt][2] - muB);
+        sc[nt][3] = exp2f(sc[nt][3] - muB);
+      }
+      lA = lA * alA + (sc[0][0] + sc[0][1] + sc[1][0] + sc[1][1]);
+      lB = lB * alB + (sc[0][2] + sc[0][3] + sc[1][2] + sc[1][3]);
+#pragma unroll
+      for (int i2 = 0; i2 < NDT; ++i2) {
+        o[i2][0] *= alA;
+        o[i2][1] *= alA;
+        o[i2][2] *= alB;
+        o[i2][3] *= alB;
+      }
+      uint32_t pa[4];
+      pa[0] = pack2<MmaT>(sc[0][0], sc[0][1]);
+      pa[1] = pack2<MmaT>(sc[0][2], sc[0][3]);
+      pa[2] = pack2<MmaT>(sc[1][0], sc[1][1]);
+      pa[3] = pack2<MmaT>(sc[1][2], sc[1][3]);
+
+      if constexpr (!C::kI8) {
+        const int mi = lane >> 3;
+        const int vtok = (mi & 1) * 8 + (lane & 7);
+#pragma unroll
+        for (int j = 0; j < D / 16; ++j) {
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4_t(swz(vt, vtok, 2 * j + (mi >> 1)), b0, b1, b2, b3);
+          mma16816<MmaT>(o[2 * j], pa, b0, b1);
+          mma16816<MmaT>(o[2 * j + 1], pa, b2, b3);
+        }
+      } else {
+        uint32_t vw[4][4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const int tok = 2 * cq + (t & 1) + (t >> 1) * 8;
+          lds128(swz(vt, tok, r), vw[t][0], vw[t][1], vw[t][2], vw[t][3]);
+        }
+        const ScaleT* vsp = reinterpret_cast<const ScaleT*>(smem + s * C::kStageBytes + 2 * C::kTileBytes + 32);
+        const __half2 vlo = __floats2half2_rn(to_f32(vsp[2 * cq]), to_f32(vsp[2 * cq + 1]));
+        const __half2 vhi = __floats2half2_rn(to_f32(vsp[2 * cq + 8]), to_f32(vsp[2 * cq + 9]));
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+          const uint32_t y01 = prmt(vw[0][w], vw[1][w], 0x5140u) ^ 0x80808080u;
+          const uint32_t y23 = prmt(vw[0][w], vw[1][w], 0x7362u) ^ 0x80808080u;
+          const uint32_t z01 = prmt(vw[2][w], vw[3][w], 0x5140u) ^ 0x80808080u;
+          const uint32_t z23 = prmt(vw[2][w], vw[3][w], 0x7362u) ^ 0x80808080u;
+          const uint32_t ys[4] = {y01, y01, y23, y23};
+          const uint32_t zs[4] = {z01, z01, z23, z23};
+#pragma unroll
+          for (int i2 = 0; i2 < 4; ++i2) {
+            const uint32_t sel = (i2 & 1) ? 0x4342u : 0x4140u;
+            uint32_t lo = i8pair_to_f16x2(ys[i2], sel), hi = i8pair_to_f16x2(zs[i2], sel);
+            __half2 lo2 = __hmul2(*reinterpret_cast<__half2*>(&lo), vlo);
+            __half2 hi2 = __hmul2(*reinterpret_cast<__half2*>(&hi), vhi);
+            mma16816<MmaT>(o[4 * w + i2], pa, *reinterpret_cast<uint32_t*>(&lo2), *reinterpret_cast<uint32_t*>(&hi2));
+          }
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[(i % NS)]);
+  }
+  // A consumer that timed out still joins the epilogue barriers below (so no other
+  // warp waits forever); its rows carry garbage and the error word is set.
+  (void)timed_out;
+
+  lA += __shfl_xor_sync(0xffffffffu, lA, 1);
+  lA += __shfl_xor_sync(0xffffffffu, lA, 2);
+  lB += __shfl_xor_sync(0xffffffffu, lB, 1);
+  lB += __shfl_xor_sync(0xffffffffu, lB, 2);
+
+  // ------------------------------------------------------------------ epilogue
+  constexpr int NCT = C::kCons * 32;
+  named_barrier(1, NCT);  // every consumer is done with the ring; reuse it
+  float* eo = reinterpret_cast<float*>(smem);  // [NWK][RB][D]
+  float* em = eo + NWK * C::kRB * D;            // [NWK][RB]
+  float* el = em + NWK * C::kRB;                // [NWK][RB]
+  {
+    const int rlA = wm * 16 + r, rlB = rlA + 8;
+#pragma unroll
+    for (int nd = 0; nd < NDT; ++nd) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int d = C::kI8 ? (32 * cq + 16 * (e & 1) + nd) : (nd * 8 + 2 * cq + (e & 1));
+        const int rl = e < 2 ? rlA : rlB;
+        eo[(wk * C::kRB + rl) * D + d] = o[nd][e];
+      }
+    }
+    if (cq == 0) {
+      em[wk * C::kRB + rlA] = mrA;
+      el[wk * C::kRB + rlA] = lA;
+      em[wk * C::kRB + rlB] = mrB;
+      el[wk * C::kRB + rlB] = lB;
+    }
+  }
+  named_barrier(1, NCT);
+  const int tid = threadIdx.x;
+  const bool single = n_chunks == 1;
+  const int64_t wsrow = (unit * p.n_chunks + c) * p.rows_real;
+  for (int64_t idx = tid; idx < rows_here * D; idx += NCT) {
+    const int rl = (int)(idx / D), d = (int)(idx % D);
+    float ms = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < NWK; ++w) ms = fmaxf(ms, em[w * C::kRB + rl]);
+    float ls = 0.f, os = 0.f;
+#pragma unroll
+    for (int w = 0; w < NWK; ++w) {
+      const float mw = em[w * C::kRB + rl];
+      if (mw != -INFINITY) {
+        const float f = exp2f(mw - ms);
+        ls += el[w * C::kRB + rl] * f;
+        os += eo[(w * C::kRB + rl) * D + d] * f;
+      }
+    }
+    if (single) {
+      store_dyn(p.out, (q_row0 + row0 + rl) * D + d, p.out_dtype, ls > 0.f ? os / ls : 0.f);
+    } else {
+      p.part_o[(wsrow + rl) * D + d] = os;
+      if (d == 0) p.part_ml[wsrow + rl] = make_float2(ms, ls);
+    }
+  }
+  if (single) return;
+
+  // Split-K: the last CTA of this unit merges every chunk's partial result.
+  __threadfence();
+  named_barrier(1, NCT);
+  if (tid == 0) {
+    const int prev = atomicAdd(&p.counters[unit], 1);
+    *s_flag = prev == (int)n_chunks - 1;
+  }
+  named_barrier(1, NCT);
+  if (!*s_flag) return;
+  __threadfence();
+  const int64_t base = unit * p.n_chunks * p.rows_real;
+  for (int64_t idx = tid; idx < rows_here * D; idx += NCT) {
+    const int rl = (int)(idx / D), d = (int)(idx % D);
+    float ms = -INFINITY;
+    for (int64_t cc = 0; cc < n_chunks; ++cc) ms = fmaxf(ms, __ldcg(&p.part_ml[base + cc * p.rows_real + rl].x));
+    float ls = 0.f, os = 0.f;
+    for (int64_t cc = 0; cc < n_chunks; ++cc) {
+      const float2 ml = __ldcg(&p.part_ml[base + cc * p.rows_real + rl]);
+      if (ml.x != -INFINITY) {
+        const float f = exp2f(ml.x - ms);
+        ls += ml.y * f;
+        os += __ldcg(&p.part_o[(base + cc * p.rows_real + rl) * D + d]) * f;
+      }
+    }
+    store_dyn(p.out, (q_row0 + row0 + rl) * D + d, p.out_dtype, ls > 0.f ? os / ls : 0.f);
+  }
+  if (tid == 0) p.counters[unit] = 0;
+}
+
+int64_t env_int(const char* name, int64_t dflt) {
+  const char* v = std::getenv(name);
+  if (v == nullptr || v[0] == '\0') return dflt;
+  return std::atoll(v);
+}
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+template <typename KvT, typename ScaleT, int D, int NWM, int NWK>
+int launch_cfg(const PagedArgs& a, const MmaPlan& plan, void* ws, cudaStream_t s) {
+  using C = Cfg<KvT, D, NWM, NWK>;
+  auto kern = paged_mma_kernel<KvT, ScaleT, D, NWM, NWK>;
+  {
+    static std::mutex mu;
+    static uint64_t done_mask = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev < 64 && !(done_mask & (1ull << dev))) {
+      int st = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes),
+                          "paged_attention: cudaFuncSetAttribute");
+      if (st != NVM_OK) return st;
+      done_mask |= 1ull << dev;
+    }
+  }
+  // Tensor maps: pools [P, Hkv, ps, D] -> dims (D, ps, Hkv, P); scales [P, Hkv, ps] -> (ps, Hkv, P).
+  const CUtensorMapDataType dt = C::kI8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                        : (std::is_same<KvT, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                                            : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16);
+  const uint64_t e = sizeof(KvT);
+  const uint64_t dims[4] = {(uint64_t)D, (uint64_t)a.page_size, (uint64_t)a.Hkv, (uint64_t)a.P};
+  const uint64_t strides[3] = {D * e, (uint64_t)a.page_size * D * e, (uint64_t)(a.Hkv * a.page_size) * D * e};
+  const uint32_t box[4] = {(uint32_t)C::kBoxElems, 16u, 1u, 1u};
+  CUtensorMap tk, tv, tks, tvs;
+  int st = encode_tmap(&tk, dt, 4, a.k_pages, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st != NVM_OK) return st;
+  st = encode_tmap(&tv, dt, 4, a.v_pages, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st != NVM_OK) return st;
+  if (C::kI8) {
+    const CUtensorMapDataType sdt =
+        std::is_same<ScaleT, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    const uint64_t sdims[3] = {(uint64_t)a.page_size, (uint64_t)a.Hkv, (uint64_t)a.P};
+    const uint64_t sstr[2] = {(uint64_t)a.page_size * 2, (uint64_t)(a.Hkv * a.page_size) * 2};
+    const uint32_t sbox[3] = {16u, 1u, 1u};
+    st = encode_tmap(&tks, sdt, 3, a.k_scales, sdims, sstr, sbox, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (st != NVM_OK) return st;
+    st = encode_tmap(&tvs, sdt, 3, a.v_scales, sdims, sstr, sbox, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (st != NVM_OK) return st;
+  } else {
+    tks = tk;
+    tvs = tv;
+  }
+  MmaParams p{};
+  p.q = a.q; p.out = a.out; p.block_table = a.block_table; p.context_lens = a.context_lens;
+  if (plan.ws_bytes > 0) {
+    char* w = static_cast<char*>(ws);
+    p.counters = reinterpret_cast<int*>(w);
+    w += align256(plan.n_units * sizeof(int));
+    p.part_ml = reinterpret_cast<float2*>(w);
+    w += align256(plan.n_units * plan.n_chunks * plan.rows_real * sizeof(float2));
+    p.part_o = reinterpret_cast<float*>(w);
+  }
+  p.err = device_error_word();
+  p.q_dtype = a.q_dtype; p.out_dtype = a.out_dtype;
+  p.B = a.B; p.Hq = a.Hq; p.Hkv = a.Hkv; p.L = a.L; p.P = a.P; p.ps = a.page_size; p.mp = a.max_pages;
+  p.dense_ctx = a.dense_ctx;
+  p.g = a.Hq / a.Hkv; p.M = p.g * a.L;
+  p.n_rb = plan.n_row_blocks; p.rows_real = plan.rows_real; p.ct = plan.chunk_tiles; p.n_chunks = plan.n_chunks;
+  p.scale_log2 = a.scale * 1.4426950408889634f;
+  p.causal = a.is_causal;
+  const dim3 grid((unsigned)plan.n_units, (unsigned)plan.n_chunks);
+  kern<<<grid, C::kThreads, C::kSmemBytes, s>>>(tk, tv, tks, tvs, p);
+  return check_cuda(cudaGetLastError(), "paged_attention: tensor-core kernel launch");
+}
+
+template <typename KvT, typename ScaleT, int D>
+int launch_d(const PagedArgs& a, const MmaPlan& plan, void* ws, cudaStream_t s) {
+  switch (plan.nwm) {
+    case 1: return launch_cfg<KvT, ScaleT, D, 1, 4>(a, plan, ws, s);
+    case 2: return launch_cfg<KvT, ScaleT, D, 2, 2>(a, plan, ws, s);
+    case 3: return launch_cfg<KvT, ScaleT, D, 3, 2>(a, plan, ws, s);
+    default: return launch_cfg<KvT, ScaleT, D, 4, 1>(a, plan, ws, s);
+  }
+}
+
+}  // namespace
+
+MmaPlan plan_paged_mma(const PagedArgs& a) {
+  MmaPlan plan{};
+  plan.eligible = false;
+  const bool kv16 = a.kv_dtype == NVM_F16 || a.kv_dtype == NVM_BF16;
+  const bool kv8 = a.kv_dtype == NVM_I8 && a.D == 128 && (a.scale_dtype == NVM_F16 || a.scale_dtype == NVM_BF16);
+  if (!(kv16 && (a.D == 64 || a.D == 128)) && !kv8) return plan;
+  const bool dense = a.dense != 0;
+  if (dense ? a.page_size < 16 : (a.page_size % 16) != 0) return plan;
+  if (a.P <= 0 || a.P > INT32_MAX || a.Hkv > INT32_MAX || a.page_size > INT32_MAX) return plan;
+  if (a.max_pages <= 0) return plan;
+  auto al16 = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
+  if (!al16(a.k_pages) || !al16(a.v_pages)) return plan;
+  if (kv8 && (!al16(a.k_scales) || !al16(a.v_scales))) return plan;
+  const int64_t M = (a.Hq / a.Hkv) * a.L;
+  plan.nwm = M <= 16 ? 1 : (M <= 32 ? 2 : (M <= 48 ? 3 : 4));
+  plan.nwk = plan.nwm == 1 ? 4 : (plan.nwm == 4 ? 1 : 2);
+  plan.rows_per_block = 16 * plan.nwm;
+  plan.n_row_blocks = (M + plan.rows_per_block - 1) / plan.rows_per_block;
+  plan.rows_real = M < plan.rows_per_block ? M : plan.rows_per_block;
+  plan.n_units = a.B * a.Hkv * plan.n_row_blocks;
+  if (plan.n_units > INT32_MAX) return plan;
+  int64_t keys = a.max_pages * a.page_size;
+  if (dense) keys = a.page_size;
+  const int64_t tiles_max = (keys + 15) / 16;
+  int64_t ct;
+  if (dense) {
+    ct = tiles_max;  // dense callers pass no workspace: never split
+  } else {
+    const int64_t target = 148 * 16;
+    ct = (plan.n_units * tiles_max + target - 1) / target;
+    ct = ((ct + 15) / 16) * 16;
+    if (ct < 16) ct = 16;
+    if (ct > kMaxChunkTiles) ct = kMaxChunkTiles;
+    const int64_t forced = env_int("NVM_ATTN_CHUNK_TILES", 0);
+    if (forced > 0) ct = forced < kMaxChunkTiles ? forced : kMaxChunkTiles;
+    if (ct > tiles_max) ct = tiles_max;
+  }
+  if (ct < 1) ct = 1;
+  if (ct > kMaxChunkTiles && !dense) ct = kMaxChunkTiles;
+  plan.chunk_tiles = ct;
+  plan.n_chunks = (tiles_max + ct - 1) / ct;
+  if (plan.n_chunks < 1) plan.n_chunks = 1;
+  if (plan.n_chunks > 65535) return plan;
+  if (dense && ct > kMaxChunkTiles) {
+    // The per-CTA page table holds kMaxChunkTiles entries; a dense sequence longer
+    // than that is still one page, so only its first entry is read -- but keep the
+    // table bound honest by splitting into several single-page chunks is not allowed
+    // without workspace.  Fall back to the generic kernel.
+    return plan;
+  }
+  plan.ws_bytes = 0;
+  if (plan.n_chunks > 1) {
+    plan.ws_bytes = align256(plan.n_units * sizeof(int)) +
+                    align256(plan.n_units * plan.n_chunks * plan.rows_real * sizeof(float2)) +
+                    (size_t)plan.n_units * plan.n_chunks * plan.rows_real * a.D * sizeof(float);
+  }
+  plan.eligible = true;
+  return plan;
+}
+
+int launch_paged_mma(const PagedArgs& a, const MmaPlan& plan, void* ws, cudaStream_t s) {
+  if (a.kv_dtype == NVM_F16) {
+    return a.D == 64 ? launch_d<__half, __half, 64>(a, plan, ws, s) : launch_d<__half, __half, 128>(a, plan, ws, s);
+  }
+  if (a.kv_dtype == NVM_BF16) {
+    return a.D == 64 ? launch_d<__nv_bfloat16, __nv_bfloat16, 64>(a, plan, ws, s)
+                     : launch_d<__nv_bfloat16, __nv_bfloat16, 128>(a, plan, ws, s);
+  }
+  if (a.scale_dtype == NVM_F16) return launch_d<int8_t, __half, 128>(a, plan, ws, s);
+  return launch_d<int8_t, __nv_bfloat16, 128>(a, plan, ws, s);
+}
+
+}  // namespace nvm

@@ -399,6 +399,9 @@ def run_ours(args):
     peaks = measured_peaks()
     cfg = decode_config(args.config)
     cfg["name"] = f"config{args.config[1]}"
+    if args.batch:
+        cfg["B"] = args.batch
+        cfg["name"] += f" (batch {args.batch})"
     w = build_decode(cfg, rank, world, device)
     torch.cuda.synchronize()
 
@@ -450,7 +453,7 @@ def run_ours(args):
     achieved = w["bytes"]["total"] / (launch_ms * 1e-3) / 1e9
     roof = dict(bound="hbm", achieved=round(achieved, 1), peak=peaks["hbm"], unit="GB/s",
                 frac=round(achieved / peaks["hbm"], 4), peak_source=peaks["src"],
-                kernel="paged_mma_kernel<bf16,D128,1x4>",
+                kernel="paged_mma_kernel (mma.sync m16n8k16, TMA-fed)",
                 algorithmic_bytes_per_launch=w["bytes"]["total"])
     tr = ncu_traffic(f"paged_mma:{args.config}:world{world}")
     roof["traffic"] = tr
@@ -459,10 +462,12 @@ def run_ours(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded; N(0,1) K/V/Q, BASELINE config distributions)",
-        "config": {"workload": f"{cfg['name']} paged decode + prefix sharing", "model": cfg["model"],
-                   "batch": cfg["B"], "q_heads": cfg["Hq"], "kv_heads": cfg["Hkv"], "head_dim": cfg["D"],
-                   "page_size": cfg["ps"], "context": "uniform[4096,32768]", "shared_prefix_tokens": 1024,
-                   "parallelism": f"kv-head shard x{world}", "l2": "inputs (19 GB) larger than L2"},
+        "config": {"workload": f"{cfg['name']} paged decode" + (" + prefix sharing" if cfg["share"] else ""),
+                   "model": cfg["model"], "batch": cfg["B"], "q_heads": cfg["Hq"], "kv_heads": cfg["Hkv"],
+                   "head_dim": cfg["D"], "page_size": cfg["ps"], "context": str(cfg["ctx"]),
+                   "shared_prefix_tokens": cfg["share"][1] if cfg["share"] else 0,
+                   "parallelism": f"kv-head shard x{world}",
+                   "l2": "inputs larger than L2" if w["bytes"]["kv"] > (256 << 20) else "inputs smaller than L2"},
         "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": round(float(et[0]), 4)},
         "gpu_launches": args.steps,
@@ -530,6 +535,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=["c1", "c3", "c4", "c5"], default="c3")
+    ap.add_argument("--batch", type=int, default=None, help="override the config's batch (small profiling cases)")
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)

@@ -98,8 +98,10 @@ int nvm_device_error(void* stream, int clear);
  * scale        softmax scale applied to q.k.
  * is_causal    row l of L may see key positions <= l + context_len - L.
  * workspace    device scratch of at least nvm_paged_attention_workspace_size(...)
- *              bytes, ZERO-FILLED before its first use; every successful call
- *              leaves it zero-filled again.  May be NULL if that size is 0.
+ *              bytes.  Its first 1 MiB holds split-K tickets: it must be zero-
+ *              filled before the first use and every successful call leaves it
+ *              zero again, so one workspace serves calls of any shape; the rest
+ *              is overwritten by every call.  May be NULL if the size is 0.
  *              Calls that share one workspace must not overlap on the GPU.
  */
 int nvm_paged_attention(const void* q, int q_dtype, const void* k_pages, const void* v_pages,

@@ -1,20 +1,532 @@
-// flash_sm100.cu -- tcgen05 / TMEM causal prefill for 16-bit Q/K/V with D == 128.
-// (Enabled once validated on B200; until then every call is served by the
-// mma.sync kernel in paged_mma.cu.)
+// flash_sm100.cu -- tcgen05 / TMEM flash attention for prefill-shaped calls:
+// dense causal (or full) prefill and chunked prefill against paged context, 16-bit
+// Q/K/V with head dim 128.
+//
+// Replaces, for L >= 64 query rows per head, the reference's FlashAttention Metal
+// kernel (flash_attention.metal:6-153, dispatch flash_attention.cpp:251-352) and
+// the multi-query paged kernel paged_attention_kv (paged_attention.metal:6-128);
+// same semantics (causal key limit row + ctx - L, holes skipped, empty rows zero).
+//
+// One CTA computes a 128-row query tile of one q head:
+//   warps 0-3  softmax: thread i owns query row i = TMEM lane i.  Reads S rows with
+//              tcgen05.ld, keeps the running max / sum in registers, writes P (bf16/
+//              f16) into shared memory in the 128B-swizzled K-major layout the tensor
+//              core reads, rescales the O accumulator in TMEM only when the row max
+//              grew by more than 2^8 (the stale max keeps every p <= 256).
+//   warp 4     producer: TMA loads of the Q tile and of 128-token K/V tiles (pages
+//              of 16 tokens for paged context, 128-row boxes for dense) into a
+//              two-stage ring; holes load an out-of-range page (zero fill).
+//   warp 5     MMA issuer: allocates 512 TMEM columns (S double buffer + O), issues
+//              S = Q K^T and O += P V as tcgen05.mma kind::f16 (M=128, N=128, fp32
+//              accumulate) from one thread, and signals completion with
+//              tcgen05.commit on mbarriers.
+// Every mbarrier wait is bounded; on expiry the CTA records an error, lets its own
+// copies and MMAs land (bounded), frees TMEM and returns.
+#include <type_traits>
+
+#include <cstdlib>
+#include <mutex>
+
 #include "nvm_common.cuh"
 #include "nvm_internal.h"
 
 namespace nvm {
+namespace {
+
+constexpr int kD = 128;          // head dim
+constexpr int kBM = 128;         // query rows per CTA
+constexpr int kBN = 128;         // keys per tile
+constexpr int kStages = 2;       // K/V ring depth
+constexpr int kTileBytes = kBN * kD * 2;  // 32 KB per K (or V) tile
+constexpr int kQBytes = kBM * kD * 2;     // 32 KB
+constexpr int kPBytes = kBM * kBN * 2;    // 32 KB
+constexpr int kThreads = 192;
+constexpr int kTmemCols = 512;
+// two P buffers: bf16 P is split into hi + lo halves (see the softmax warps)
+constexpr int kSmemBytes = 1024 + kQBytes + kStages * 2 * kTileBytes + 2 * kPBytes + 256;
+constexpr float kRescaleThreshold = 8.0f;  // log2(256)
+
+struct Sm100Params {
+  void* out;
+  const int32_t* block_table;
+  const int32_t* context_lens;
+  int* err;
+  int out_dtype;
+  int64_t B, Hq, Hkv, L, P, ps, mp, dense_ctx;
+  int64_t n_row_tiles;
+  float scale_log2;
+  int causal;
+  int dense;
+  int box_rows;   // rows of one K/V TMA box: 16 (pages) or 128 (dense)
+};
+
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  // start >>4 [0,14), LBO>>4 [16,30), SBO>>4 [32,46), version 1 at [46,48), layout SWIZZLE_128B (2) at [61,64)
+  return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// kind::f16 instruction descriptor: f32 accumulator, A/B format, K-major A, B major
+// as given, N >> 3 at [17,23), M >> 4 at [24,29).
+template <typename T>
+__device__ __forceinline__ uint32_t idesc(bool b_mn_major) {
+  const uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
+  return (1u << 4) | (fmt << 7) | (fmt << 10) | ((b_mn_major ? 1u : 0u) << 16) | ((uint32_t)(kBN >> 3) << 17) |
+         ((uint32_t)(kBM >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t id, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(da), "l"(db), "r"(id), "r"(acc)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t* r = reinterpret_cast<uint32_t*>(v);
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+  const uint32_t* r = reinterpret_cast<const uint32_t*>(v);
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]),
+      "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]),
+      "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+// Every lane waits; the result is the same on all lanes (tcgen05.ld/st need a converged warp).
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
+  const bool ok = mbar_wait(bar, parity);
+  return __all_sync(0xffffffffu, ok) != 0;
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1)
+    flash_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                       const __grid_constant__ CUtensorMap tm_v, const Sm100Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sKV = sQ + kQBytes;                       // stage s: K at s*64K, V at s*64K + 32K
+  uint8_t* sP = sKV + kStages * 2 * kTileBytes;
+  uint8_t* sPlo = sP + kPBytes;                      // bf16 only: p - bf16(p)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * kPBytes);
+  constexpr bool kSplit = std::is_same<T, __nv_bfloat16>::value;
+  uint64_t* q_full = bars + 0;
+  uint64_t* kv_full = bars + 1;                 // [kStages]
+  uint64_t* kv_empty = bars + 1 + kStages;      // [kStages]
+  uint64_t* s_full = bars + 1 + 2 * kStages;    // [2]
+  uint64_t* p_full = bars + 3 + 2 * kStages;    // 1 (count 128)
+  uint64_t* o_done = bars + 4 + 2 * kStages;    // 1: PV_j complete
+  uint64_t* mma_done = bars + 5 + 2 * kStages;  // 1: every MMA of the CTA complete (teardown)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8 + 2 * kStages);
+  int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // heavy (late, causal) row tiles first
+  const int64_t rt = p.n_row_tiles - 1 - (int64_t)(blockIdx.x % p.n_row_tiles);
+  const int64_t n = blockIdx.x / p.n_row_tiles;  // flat (b, q head)
+  const int64_t b = n / p.Hq, qh = n % p.Hq;
+  const int64_t kvh = qh / (p.Hq / p.Hkv);
+  const int64_t ctx = p.dense ? p.dense_ctx : (int64_t)p.context_lens[b];
+  const int64_t cap = p.mp * p.ps;
+  const int64_t ctx_limit = ctx < cap ? ctx : cap;
+  const int64_t l0 = rt * kBM;
+  const int64_t rows = (p.L - l0) < kBM ? (p.L - l0) : kBM;
+  int64_t need = ctx_limit;
+  if (p.causal) {
+    const int64_t lim = (l0 + rows - 1) + ctx - p.L + 1;
+    if (lim < need) need = lim;
+  }
+  if (ctx <= 0 || need < 0) need = 0;
+  const int n_tiles = (int)((need + kBN - 1) / kBN);
+  // keys below `clean` are visible to every row of the tile
+  int64_t clean = ctx_limit;
+  if (p.causal) {
+    const int64_t lim0 = l0 + ctx - p.L + 1;
+    if (lim0 < clean) clean = lim0;
+  }
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    mbar_init(&s_full[0], 1);
+    mbar_init(&s_full[1], 1);
+    mbar_init(p_full, 128);
+    mbar_init(o_done, 1);
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 5) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS[2] = {tmem, tmem + 128};
+  const uint32_t tO = tmem + 256;
+
+  if (warp == 4) {
+    // ---------------------------------------------------------------- producer
+    int issued = 0;
+    if (n_tiles > 0) {
+      if (lane == 0) {
+        prefetch_tmap(&tm_q);
+        prefetch_tmap(&tm_k);
+        prefetch_tmap(&tm_v);
+        mbar_arrive_expect_tx(q_full, kQBytes);
+        tma_load_3d(sQ, &tm_q, 0, (int)l0, (int)n, q_full);
+        tma_load_3d(sQ + kBM * 128, &tm_q, 64, (int)l0, (int)n, q_full);
+      }
+      const int boxes = kBN / p.box_rows;  // K/V boxes per 64-column half
+      for (int j = 0; j < n_tiles; ++j) {
+        const int s = j % kStages;
+        bool ok = true;
+        if (j >= kStages) ok = mbar_wait(&kv_empty[s], ((j / kStages) & 1) ^ 1);
+        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+        if (!ok || *(volatile int*)abort_flag) {
+          if (lane == 0) {
+            record_error(p.err, kDevErrEmptyWait);
+            *(volatile int*)abort_flag = 1;
+          }
+          break;
+        }
+        if (lane == 0) mbar_arrive_expect_tx(&kv_full[s], 2 * kTileBytes);
+        __syncwarp();
+        uint8_t* sk = sKV + s * 2 * kTileBytes;
+        uint8_t* sv = sk + kTileBytes;
+        // lanes issue the boxes of this tile: (half, box) pairs for K and V
+        for (int t = lane; t < 2 * boxes; t += 32) {
+          const int half = t / boxes, bx = t % boxes;
+          const int64_t tok0 = (int64_t)j * kBN + (int64_t)bx * p.box_rows;
+          int pid, slot0;
+          if (p.dense) {
+            pid = (int)b;
+            slot0 = (int)tok0;
+          } else {
+            const int64_t pidx = tok0 / p.ps;
+            int64_t id = pidx < p.mp ? (int64_t)p.block_table[b * p.mp + pidx] : -1;
+            if (id < 0 || id >= p.P) id = p.P;  // hole: out-of-range page, TMA fills zeros
+            pid = (int)id;
+            slot0 = (int)(tok0 % p.ps);
+          }
+          const uint32_t off = (uint32_t)(half * kBN * 128 + bx * p.box_rows * 128);
+          tma_load_4d(sk + off, &tm_k, half * 64, slot0, (int)kvh, pid, &kv_full[s]);
+          tma_load_4d(sv + off, &tm_v, half * 64, slot0, (int)kvh, pid, &kv_full[s]);
+        }
+        issued = j + 1;
+      }
+      // drain: every issued load must land before the CTA may exit
+      if (lane == 0) {
+        if (!mbar_wait(q_full, 0)) record_error(p.err, kDevErrDrainWait);
+        for (int s = 0; s < kStages && s < issued; ++s) {
+          const int last = s + ((issued - 1 - s) / kStages) * kStages;
+          if (!mbar_wait(&kv_full[s], (last / kStages) & 1)) record_error(p.err, kDevErrDrainWait);
+        }
+      }
+    }
+  } else if (warp == 5) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (n_tiles > 0 && lane == 0) {
+      const uint32_t id_qk = idesc<T>(false);
+      const uint32_t id_pv = idesc<T>(true);
+      const uint32_t q_addr = smem_u32(sQ), p_addr = smem_u32(sP), plo_addr = smem_u32(sPlo);
+      bool ok = mbar_wait(q_full, 0);
+      auto issue_s = [&](int j) -> bool {
+        const int s = j % kStages;
+        if (!mbar_wait(&kv_full[s], (j / kStages) & 1)) return false;
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(sKV + s * 2 * kTileBytes);
+#pragma unroll
+        for (int ks = 0; ks < kD / 16; ++ks) {
+          const uint32_t koff = (uint32_t)((ks >> 2) * (kBM * 128) + (ks & 3) * 32);
+          const uint64_t da = smem_desc(q_addr + koff, 16, 1024);
+          const uint64_t db = smem_desc(k_addr + (uint32_t)((ks >> 2) * (kBN * 128) + (ks & 3) * 32), 16, 1024);
+          mma_f16(tS[j & 1], da, db, id_qk, ks > 0 ? 1u : 0u);
+        }
+        mma_commit(&s_full[j & 1]);
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      if (ok && n_tiles > 1) ok = issue_s(1);
+      for (int j = 0; ok && j < n_tiles; ++j) {
+        // P_j written by the softmax warps (which also finished reading S_j)
+        if (!mbar_wait(p_full, j & 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const int s = j % kStages;
+        const uint32_t v_addr = smem_u32(sKV + s * 2 * kTileBytes + kTileBytes);
+#pragma unroll
+        for (int ks = 0; ks < kBN / 16; ++ks) {
+          const uint32_t poff = (uint32_t)((ks >> 2) * (kBM * 128) + (ks & 3) * 32);
+          // V is MN-major: 64-column halves kBN*128 bytes apart (LBO), 8-token groups 1024 apart (SBO)
+          const uint64_t db = smem_desc(v_addr + (uint32_t)(ks * 16 * 128), kBN * 128, 1024);
+          mma_f16(tO, smem_desc(p_addr + poff, 16, 1024), db, id_pv, (j > 0 || ks > 0) ? 1u : 0u);
+          if (kSplit) mma_f16(tO, smem_desc(plo_addr + poff, 16, 1024), db, id_pv, 1u);
+        }
+        mma_commit(o_done);
+        mma_commit(&kv_empty[s]);
+        if (j + 2 < n_tiles) ok = issue_s(j + 2);
+      }
+      if (!ok) {
+        record_error(p.err, kDevErrMmaWait);
+        *(volatile int*)abort_flag = 1;
+      }
+      // arrives once every MMA issued by this thread has finished (TMEM teardown)
+      mma_commit(mma_done);
+    }
+  } else {
+    // ---------------------------------------------------------------- softmax warps 0-3
+    const int row = warp * 32 + lane;            // TMEM lane == query row in the tile
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    const int64_t lrow = l0 + row;               // query index
+    const bool row_ok = row < rows;
+    const int64_t lim = p.causal ? (lrow + ctx - p.L) : INT64_MAX / 4;  // last visible key
+    float m = -INFINITY, lsum = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_tiles; ++j) {
+      if (!warp_wait(&s_full[j & 1], (j >> 1) & 1)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float sv[kBN];
+#pragma unroll
+      for (int c = 0; c < kBN / 32; ++c) tmem_ld32(tS[j & 1] + lane_base + c * 32, *reinterpret_cast<float(*)[32]>(&sv[c * 32]));
+      tmem_wait_ld();
+      const int64_t key0 = (int64_t)j * kBN;
+      const bool need_mask = key0 + kBN > clean || !row_ok;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < kBN; ++c) {
+        float x = sv[c] * p.scale_log2;
+        if (need_mask) {
+          const int64_t key = key0 + c;
+          if (key >= ctx_limit || key > lim) x = -INFINITY;
+        }
+        sv[c] = x;
+        mx = fmaxf(mx, x);
+      }
+      // holes: whole 16-token groups of missing pages are masked
+      if (!p.dense) {
+#pragma unroll
+        for (int g = 0; g < kBN / 16; ++g) {
+          const int64_t pidx = (key0 + g * 16) / p.ps;
+          const int64_t id = pidx < p.mp ? (int64_t)p.block_table[b * p.mp + pidx] : -1;
+          if (id < 0 || id >= p.P) {
+#pragma unroll
+            for (int c = 0; c < 16; ++c) sv[g * 16 + c] = -INFINITY;
+          }
+        }
+        mx = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < kBN; ++c) mx = fmaxf(mx, sv[c]);
+      }
+      // lazy max: keep the old reference max unless the new one exceeds it by > 8
+      float m_ref = m;
+      bool rescale = false;
+      if (mx > -INFINITY && (m == -INFINITY || mx > m + kRescaleThreshold)) {
+        rescale = m != -INFINITY;
+        m_ref = mx;
+      }
+      const float mu = m_ref == -INFINITY ? 0.f : m_ref;
+      const float alpha = exp2f(m - mu);  // 0 when m == -inf
+      float rs = 0.f;
+#pragma unroll
+      for (int c = 0; c < kBN; ++c) {
+        sv[c] = exp2f(sv[c] - mu);
+        rs += sv[c];
+      }
+      lsum = (m == -INFINITY ? 0.f : lsum * alpha) + rs;
+      m = m_ref;
+      // wait until PV_{j-1} finished: P buffers free, O stable for rescaling
+      if (j > 0) {
+        if (!warp_wait(o_done, (j - 1) & 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, rescale)) {
+          const float f = rescale ? alpha : 1.f;
+#pragma unroll 1
+          for (int c = 0; c < kD / 32; ++c) {
+            float ov[32];
+            tmem_ld32(tO + lane_base + c * 32, ov);
+            tmem_wait_ld();
+#pragma unroll
+            for (int x = 0; x < 32; ++x) ov[x] *= f;
+            tmem_st32(tO + lane_base + c * 32, ov);
+          }
+          tmem_wait_st();
+        }
+      }
+      // P row -> shared memory, 128B-swizzled K-major: atom a = key/64, chunk c = (key%64)/8
+      const int rswz = row & 7;
+#pragma unroll
+      for (int ch = 0; ch < kBN / 8; ++ch) {
+        const int a = ch >> 3, c = ch & 7;
+        const uint32_t off = (uint32_t)(a * (kBM * 128) + row * 128 + ((c ^ rswz) << 4));
+        uint32_t hi[4];
+#pragma unroll
+        for (int x = 0; x < 4; ++x) hi[x] = pack2<T>(sv[ch * 8 + 2 * x], sv[ch * 8 + 2 * x + 1]);
+        *reinterpret_cast<uint4*>(sP + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        if constexpr (kSplit) {
+          uint32_t lo[4];
+#pragma unroll
+          for (int x = 0; x < 4; ++x) {
+            const __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&hi[x]);
+            lo[x] = pack2<T>(sv[ch * 8 + 2 * x] - __low2float(h), sv[ch * 8 + 2 * x + 1] - __high2float(h));
+          }
+          *reinterpret_cast<uint4*>(sPlo + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        }
+      }
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    // final O: wait for the last PV, normalise, store
+    if (ok && n_tiles > 0 && !warp_wait(o_done, (n_tiles - 1) & 1)) ok = false;
+    if (!ok) {
+      record_error(p.err, kDevErrFullWait);
+      *(volatile int*)abort_flag = 1;
+    }
+    tc_fence_after();
+    const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+    const int64_t orow = (n * p.L + lrow) * kD;
+#pragma unroll 1
+    for (int c = 0; c < kD / 32; ++c) {
+      float ov[32];
+      if (n_tiles > 0) {
+        tmem_ld32(tO + lane_base + c * 32, ov);
+        tmem_wait_ld();
+      } else {
+#pragma unroll
+        for (int x = 0; x < 32; ++x) ov[x] = 0.f;
+      }
+      if (row_ok) {
+#pragma unroll
+        for (int x = 0; x < 32; ++x) store_dyn(p.out, orow + c * 32 + x, p.out_dtype, ov[x] * inv);
+      }
+    }
+  }
+
+  // ------------------------------------------------------------------ teardown
+  if (warp == 5 && lane == 0 && n_tiles > 0) {
+    if (!mbar_wait(mma_done, 0)) record_error(p.err, kDevErrMmaWait);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 5) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+}
+
+// One opt-in to the 225 KB dynamic shared memory per kernel instantiation and device.
+template <typename T>
+int launch_typed(dim3 grid, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                 const Sm100Params& p, cudaStream_t s) {
+  static std::mutex mu;
+  static uint64_t done = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev < 64 && !(done & (1ull << dev))) {
+      int r = check_cuda(cudaFuncSetAttribute(flash_sm100_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              kSmemBytes),
+                         "flash_attention: cudaFuncSetAttribute");
+      if (r != NVM_OK) return r;
+      done |= 1ull << dev;
+    }
+  }
+  flash_sm100_kernel<T><<<grid, kThreads, kSmemBytes, s>>>(tq, tk, tv, p);
+  return check_cuda(cudaGetLastError(), "flash_attention: sm100 kernel launch");
+}
+
+}  // namespace
 
 bool sm100_prefill_eligible(const PagedArgs& a) {
-  (void)a;
-  return false;
+  if (a.kv_dtype != NVM_F16 && a.kv_dtype != NVM_BF16) return false;
+  if (a.q_dtype != a.kv_dtype) return false;
+  if (a.D != kD) return false;
+  if (a.L < 64) return false;
+  if (a.dense) {
+    if (a.page_size < kBN) return false;  // dense boxes are 128 rows
+  } else if (a.page_size != 16) {
+    return false;
+  }
+  if (a.P <= 0 || a.P >= INT32_MAX || a.B * a.Hq > INT32_MAX) return false;
+  auto al16 = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
+  return al16(a.q) && al16(a.k_pages) && al16(a.v_pages);
 }
 
 int launch_sm100_prefill(const PagedArgs& a, cudaStream_t s) {
-  (void)a;
-  (void)s;
-  return fail(NVM_ERR_UNSUPPORTED, "flash_attention: sm100 prefill kernel not built");
-}
+  const CUtensorMapDataType dt = a.kv_dtype == NVM_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  // Q [B*Hq, L, D] -> (D, L, B*Hq), 64 x 128 boxes
+  const uint64_t qd[3] = {(uint64_t)kD, (uint64_t)a.L, (uint64_t)(a.B * a.Hq)};
+  const uint64_t qs[2] = {kD * 2, (uint64_t)a.L * kD * 2};
+  const uint32_t qb[3] = {64u, (uint32_t)kBM, 1u};
+  CUtensorMap tq, tk, tv;
+  int st = encode_tmap(&tq, dt, 3, a.q, qd, qs, qb, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st != NVM_OK) return st;
+  // pools [P, Hkv, ps, D] -> (D, ps, Hkv, P)
+  const int box_rows = a.dense ? kBN : 16;
+  const uint64_t kd[4] = {(uint64_t)kD, (uint64_t)a.page_size, (uint64_t)a.Hkv, (uint64_t)a.P};
+  const uint64_t ks[3] = {kD * 2, (uint64_t)a.page_size * kD * 2, (uint64_t)(a.Hkv * a.page_size) * kD * 2};
+  const uint32_t kb[4] = {64u, (uint32_t)box_rows, 1u, 1u};
+  st = encode_tmap(&tk, dt, 4, a.k_pages, kd, ks, kb, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st != NVM_OK) return st;
+  st = encode_tmap(&tv, dt, 4, a.v_pages, kd, ks, kb, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st != NVM_OK) return st;
 
+  Sm100Params p{};
+  p.out = a.out; p.block_table = a.block_table; p.context_lens = a.context_lens; p.err = device_error_word();
+  p.out_dtype = a.out_dtype;
+  p.B = a.B; p.Hq = a.Hq; p.Hkv = a.Hkv; p.L = a.L; p.P = a.P; p.ps = a.page_size; p.mp = a.max_pages;
+  p.dense_ctx = a.dense_ctx;
+  p.n_row_tiles = (a.L + kBM - 1) / kBM;
+  p.scale_log2 = a.scale * 1.4426950408889634f;
+  p.causal = a.is_causal; p.dense = a.dense; p.box_rows = box_rows;
+
+  const dim3 grid((unsigned)(a.B * a.Hq * p.n_row_tiles));
+  if (a.kv_dtype == NVM_F16) return launch_typed<__half>(grid, tq, tk, tv, p, s);
+  return launch_typed<__nv_bfloat16>(grid, tq, tk, tv, p, s);
+}
 }  // namespace nvm

@@ -37,6 +37,10 @@ namespace nvm {
 namespace {
 
 constexpr int kMaxChunkTiles = 256;
+// Split-K tickets live in a fixed region at the start of the workspace that partial
+// results never use, so one zero-filled workspace can serve calls of any shape.
+constexpr size_t kCounterBytes = 1 << 20;
+constexpr int64_t kMaxUnits = (int64_t)(kCounterBytes / sizeof(int));
 
 struct MmaParams {
   const void* q;
@@ -59,11 +63,13 @@ template <typename KvT, int D, int NWM, int NWK>
 struct Cfg {
   static constexpr bool kI8 = std::is_same<KvT, int8_t>::value;
   using MmaT = typename std::conditional<kI8, __half, KvT>::type;
+  static constexpr bool kSplitP = std::is_same<KvT, __nv_bfloat16>::value;
   static constexpr int kCons = NWM * NWK;
   static constexpr int kThreads = (kCons + 1) * 32;
   static constexpr int kRB = 16 * NWM;
   static constexpr int kTileBytes = 16 * D * (int)sizeof(KvT);
-  static constexpr int kScaleBytes = kI8 ? 64 : 0;
+  // K scales at +0, V scales at +128 past the two tiles: TMA destinations are 128-byte aligned.
+  static constexpr int kScaleBytes = kI8 ? 256 : 0;
   static constexpr int kStageBytes = ((2 * kTileBytes + kScaleBytes + 1023) / 1024) * 1024;
   static constexpr int kStages = kI8 ? 12 : 8;
   static constexpr int kBoxElems = 128 / (int)sizeof(KvT);  // 128-byte inner box (swizzle span)
@@ -76,6 +82,12 @@ struct Cfg {
   static_assert(D % 64 == 0, "head dim must be 64 or 128");
   static_assert(!kI8 || D == 128, "int8 path needs D == 128");
 };
+
+// bf16 pair of the rounding residuals (a - hi.x, b - hi.y) of a packed bf16 pair.
+__device__ __forceinline__ uint32_t pack_residual(float a, float b, uint32_t hi) {
+  const __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&hi);
+  return pack2<__nv_bfloat16>(a - __low2float(h), b - __high2float(h));
+}
 
 // Address of 16-byte chunk `q` of token row `tok` inside a TMA tile written with
 // 128-byte swizzle: boxes of 128 bytes x 16 rows, 2048 bytes each, chunk index XOR row.
@@ -168,7 +180,7 @@ __global__ void __launch_bounds__(Cfg<KvT, D, NWM, NWK>::kThreads)
         if (pid >= 0) {
           const int slot0 = (int)(((t_begin + i) * 16) % p.ps);
           uint8_t* st = smem + s * C::kStageBytes;
-          mbar_arrive_expect_tx(&full[s], 2 * C::kTileBytes + C::kScaleBytes);
+          mbar_arrive_expect_tx(&full[s], 2 * C::kTileBytes + (C::kI8 ? 64 : 0));
 #pragma unroll
           for (int hb = 0; hb < C::kBoxes; ++hb) {
             tma_load_4d(st + hb * 2048, &tm_k, hb * C::kBoxElems, slot0, (int)h, pid, &full[s]);
@@ -176,7 +188,7 @@ __global__ void __launch_bounds__(Cfg<KvT, D, NWM, NWK>::kThreads)
           }
           if (C::kI8) {
             tma_load_3d(st + 2 * C::kTileBytes, &tm_ks, slot0, (int)h, pid, &full[s]);
-            tma_load_3d(st + 2 * C::kTileBytes + 32, &tm_vs, slot0, (int)h, pid, &full[s]);
+            tma_load_3d(st + 2 * C::kTileBytes + 128, &tm_vs, slot0, (int)h, pid, &full[s]);
           }
         } else {
           mbar_arrive(&full[s]);
@@ -342,11 +354,19 @@ __global__ void __launch_bounds__(Cfg<KvT, D, NWM, NWK>::kThreads)
         o[i2][2] *= alB;
         o[i2][3] *= alB;
       }
-      uint32_t pa[4];
+      uint32_t pa[4], pl[4];
       pa[0] = pack2<MmaT>(sc[0][0], sc[0][1]);
       pa[1] = pack2<MmaT>(sc[0][2], sc[0][3]);
       pa[2] = pack2<MmaT>(sc[1][0], sc[1][1]);
       pa[3] = pack2<MmaT>(sc[1][2], sc[1][3]);
+      if constexpr (C::kSplitP) {
+        // bf16 keeps 8 mantissa bits; the residual p - bf16(p) is a second bf16
+        // operand so P reaches the tensor core with ~16 bits.
+        pl[0] = pack_residual(sc[0][0], sc[0][1], pa[0]);
+        pl[1] = pack_residual(sc[0][2], sc[0][3], pa[1]);
+        pl[2] = pack_residual(sc[1][0], sc[1][1], pa[2]);
+        pl[3] = pack_residual(sc[1][2], sc[1][3], pa[3]);
+      }
 
       if constexpr (!C::kI8) {
         const int mi = lane >> 3;
@@ -357,6 +377,10 @@ __global__ void __launch_bounds__(Cfg<KvT, D, NWM, NWK>::kThreads)
           ldsm_x4_t(swz(vt, vtok, 2 * j + (mi >> 1)), b0, b1, b2, b3);
           mma16816<MmaT>(o[2 * j], pa, b0, b1);
           mma16816<MmaT>(o[2 * j + 1], pa, b2, b3);
+          if constexpr (C::kSplitP) {
+            mma16816<MmaT>(o[2 * j], pl, b0, b1);
+            mma16816<MmaT>(o[2 * j + 1], pl, b2, b3);
+          }
         }
       } else {
         uint32_t vw[4][4];
@@ -365,7 +389,7 @@ __global__ void __launch_bounds__(Cfg<KvT, D, NWM, NWK>::kThreads)
           const int tok = 2 * cq + (t & 1) + (t >> 1) * 8;
           lds128(swz(vt, tok, r), vw[t][0], vw[t][1], vw[t][2], vw[t][3]);
         }
-        const ScaleT* vsp = reinterpret_cast<const ScaleT*>(smem + s * C::kStageBytes + 2 * C::kTileBytes + 32);
+        const ScaleT* vsp = reinterpret_cast<const ScaleT*>(smem + s * C::kStageBytes + 2 * C::kTileBytes + 128);
         const __half2 vlo = __floats2half2_rn(to_f32(vsp[2 * cq]), to_f32(vsp[2 * cq + 1]));
         const __half2 vhi = __floats2half2_rn(to_f32(vsp[2 * cq + 8]), to_f32(vsp[2 * cq + 9]));
 #pragma unroll
@@ -537,7 +561,7 @@ int launch_cfg(const PagedArgs& a, const MmaPlan& plan, void* ws, cudaStream_t s
   if (plan.ws_bytes > 0) {
     char* w = static_cast<char*>(ws);
     p.counters = reinterpret_cast<int*>(w);
-    w += align256(plan.n_units * sizeof(int));
+    w += kCounterBytes;
     p.part_ml = reinterpret_cast<float2*>(w);
     w += align256(plan.n_units * plan.n_chunks * plan.rows_real * sizeof(float2));
     p.part_o = reinterpret_cast<float*>(w);
@@ -588,11 +612,12 @@ MmaPlan plan_paged_mma(const PagedArgs& a) {
   plan.rows_real = M < plan.rows_per_block ? M : plan.rows_per_block;
   plan.n_units = a.B * a.Hkv * plan.n_row_blocks;
   if (plan.n_units > INT32_MAX) return plan;
+  const bool can_split = plan.n_units <= kMaxUnits;
   int64_t keys = a.max_pages * a.page_size;
   if (dense) keys = a.page_size;
   const int64_t tiles_max = (keys + 15) / 16;
   int64_t ct;
-  if (dense) {
+  if (dense || !can_split) {
     ct = tiles_max;  // dense callers pass no workspace: never split
   } else {
     const int64_t target = 148 * 16;
@@ -619,8 +644,7 @@ MmaPlan plan_paged_mma(const PagedArgs& a) {
   }
   plan.ws_bytes = 0;
   if (plan.n_chunks > 1) {
-    plan.ws_bytes = align256(plan.n_units * sizeof(int)) +
-                    align256(plan.n_units * plan.n_chunks * plan.rows_real * sizeof(float2)) +
+    plan.ws_bytes = kCounterBytes + align256(plan.n_units * plan.n_chunks * plan.rows_real * sizeof(float2)) +
                     (size_t)plan.n_units * plan.n_chunks * plan.rows_real * a.D * sizeof(float);
   }
   plan.eligible = true;

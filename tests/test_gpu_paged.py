@@ -154,6 +154,19 @@ def test_split_k_combine(cuda, oracle, kvd, monkeypatch):
     assert nv.device_error(cuda) == 0
 
 
+def test_workspace_shared_across_shapes(cuda, oracle):
+    """One cached workspace serves split-K calls of different shapes back to back."""
+    gen = torch.Generator().manual_seed(21)
+    probs = [random_paged_problem(gen, 16, 16, 8, 1, 128, 16, torch.float16, 128, 1024, spare_pages=64),
+             random_paged_problem(gen, 40, 32, 8, 1, 128, 16, torch.bfloat16, 1000, 3000),
+             random_paged_problem(gen, 3, 64, 8, 1, 128, 16, torch.int8, 2000, 5000)]
+    for prob in probs + probs[::-1]:
+        out = paged_attention(prob["q"], prob["kp"], prob["vp"], prob["bt"], prob["cl"], 16, prob["ks"], prob["vs"],
+                              mask="causal")
+        assert_close(out, oracle_paged(oracle, prob), TOL16)
+    assert nv.device_error(cuda) == 0
+
+
 def test_context_clipped_to_block_table(cuda, oracle):
     gen = torch.Generator().manual_seed(4)
     prob = random_paged_problem(gen, 3, 8, 2, 1, 128, 16, torch.float16, 40, 100)

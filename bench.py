@@ -229,7 +229,9 @@ class ClockSampler:
 
 
 def flush_l2(buf: torch.Tensor):
-    buf.add_(1)  # writes > L2 (126 MB) so the next launch starts cold
+    # Read (not write) > L2 (126 MB): evicts the previous launch's lines without
+    # leaving dirty lines whose write-back would be charged to the next launch.
+    buf.view(torch.int32).sum(dtype=torch.int32)
 
 
 def time_launches(fn, iters: int, warmup: int, flush_buf=None) -> list[float]:
@@ -384,8 +386,42 @@ def secondary_results(peaks: dict, device) -> list[dict]:
     return res
 
 
+def run_prefill(args):
+    """Config 2a: dense causal prefill (flash_attention), bf16, TFLOPS of visible pairs."""
+    from nano_vllm_b200 import flash_attention
+    from nano_vllm_b200 import _native as nv
+
+    device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(device)
+    peaks = measured_peaks()
+    B = args.batch or 4
+    Hq, Hkv, L, D = 32, 8, 2048, 128
+    gen = torch.Generator(device=device)
+    gen.manual_seed(5)
+    q = torch.randn(B, Hq, L, D, generator=gen, device=device).bfloat16()
+    k = torch.randn(B, Hkv, L, D, generator=gen, device=device).bfloat16()
+    v = torch.randn(B, Hkv, L, D, generator=gen, device=device).bfloat16()
+    flops = 4 * D * Hq * B * (L * (L + 1) // 2)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    times = time_launches(lambda: flash_attention(q, k, v, mask="causal", out_dtype=torch.bfloat16), args.steps,
+                          args.warmup, flush)
+    ms = statistics.median(times)
+    tf = flops / (ms * 1e-3) / 1e12
+    line = {"metric": "prefill attn TFLOPS", "value": round(tf, 1), "unit": "TFLOP/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+            "dtype": "bf16", "config": {"workload": f"config2a dense causal prefill {B}x{L}, 32q/8kv, d128",
+                                        "l2": "flushed between launches"},
+            "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": peaks["bf16"], "unit": "TFLOP/s",
+                         "frac": round(tf / peaks["bf16"], 4), "peak_source": peaks["src"]},
+            "device_error_word": nv.device_error(device)}
+    print(json.dumps(line), flush=True)
+
+
 def run_ours(args):
     import torch.distributed as dist
+
+    if args.config == "c2a":
+        return run_prefill(args)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -534,7 +570,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["c1", "c3", "c4", "c5"], default="c3")
+    ap.add_argument("--config", choices=["c1", "c2a", "c3", "c4", "c5"], default="c3")
     ap.add_argument("--batch", type=int, default=None, help="override the config's batch (small profiling cases)")
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")

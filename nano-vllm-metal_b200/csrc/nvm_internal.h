@@ -68,6 +68,7 @@ struct MmaPlan {
   bool eligible;   // shapes/dtypes/alignment served by the tensor-core kernel
   int nwm;         // 16-row m-tiles per CTA (warps along rows)
   int nwk;         // warps splitting the key tiles of one CTA
+  int variant;     // decode kernel variant (consumer warps x stage depth)
   int rows_per_block;
   int64_t n_row_blocks;
   int64_t rows_real;      // rows of one (seq, kv head) unit actually stored per block

@@ -41,6 +41,8 @@ constexpr int kMaxChunkTiles = 256;
 // results never use, so one zero-filled workspace can serve calls of any shape.
 constexpr size_t kCounterBytes = 1 << 20;
 constexpr int64_t kMaxUnits = (int64_t)(kCounterBytes / sizeof(int));
+constexpr int kDefaultDecodeVariant = 3;  // c4 int8 prefers 4 (2 warps, 8 stages) by 1%
+constexpr int kDefaultM3Variant = 1;
 
 struct MmaParams {
   const void* q;
@@ -59,7 +61,7 @@ struct MmaParams {
   int causal;
 };
 
-template <typename KvT, int D, int NWM, int NWK>
+template <typename KvT, int D, int NWM, int NWK, int NS_ = 0>
 struct Cfg {
   static constexpr bool kI8 = std::is_same<KvT, int8_t>::value;
   using MmaT = typename std::conditional<kI8, __half, KvT>::type;
@@ -71,7 +73,7 @@ struct Cfg {
   // K scales at +0, V scales at +128 past the two tiles: TMA destinations are 128-byte aligned.
   static constexpr int kScaleBytes = kI8 ? 256 : 0;
   static constexpr int kStageBytes = ((2 * kTileBytes + kScaleBytes + 1023) / 1024) * 1024;
-  static constexpr int kStages = kI8 ? 12 : 8;
+  static constexpr int kStages = NS_ > 0 ? NS_ : (kI8 ? 12 : 8);
   static constexpr int kBoxElems = 128 / (int)sizeof(KvT);  // 128-byte inner box (swizzle span)
   static constexpr int kBoxes = D / kBoxElems;
   static constexpr int kEpiBytes = NWK * kRB * D * 4 + 2 * NWK * kRB * 4;
@@ -95,12 +97,12 @@ __device__ __forceinline__ uint32_t swz(uint32_t tile, int tok, int q) {
   return tile + (uint32_t)((q >> 3) * 2048 + tok * 128 + (((q & 7) ^ (tok & 7)) << 4));
 }
 
-template <typename KvT, typename ScaleT, int D, int NWM, int NWK>
-__global__ void __launch_bounds__(Cfg<KvT, D, NWM, NWK>::kThreads)
+template <typename KvT, typename ScaleT, int D, int NWM, int NWK, int NS_>
+__global__ void __launch_bounds__(Cfg<KvT, D, NWM, NWK, NS_>::kThreads)
     paged_mma_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                      const __grid_constant__ CUtensorMap tm_ks, const __grid_constant__ CUtensorMap tm_vs,
                      const MmaParams p) {
-  using C = Cfg<KvT, D, NWM, NWK>;
+  using C = Cfg<KvT, D, NWM, NWK, NS_>;
   using MmaT = typename C::MmaT;
   constexpr int NS = C::kStages;
   constexpr int NKS = D / 16;  // k-steps of Q K^T
@@ -276,15 +278,28 @@ __global__ void __launch_bounds__(Cfg<KvT, D, NWM, NWK>::kThreads)
       for (int nt = 0; nt < 2; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
 
       if constexpr (!C::kI8) {
+        // two accumulator sets (even / odd k-steps) halve the dependent mma chain
+        float sd[2][4];
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) sd[nt][0] = sd[nt][1] = sd[nt][2] = sd[nt][3] = 0.f;
         const int mi = lane >> 3;
         const int ktok = (mi >> 1) * 8 + (lane & 7);
 #pragma unroll
         for (int ks = 0; ks < NKS; ++ks) {
           uint32_t b0, b1, b2, b3;
           ldsm_x4(swz(kt, ktok, 2 * ks + (mi & 1)), b0, b1, b2, b3);
-          mma16816<MmaT>(sc[0], qa[ks], b0, b1);
-          mma16816<MmaT>(sc[1], qa[ks], b2, b3);
+          if (ks & 1) {
+            mma16816<MmaT>(sd[0], qa[ks], b0, b1);
+            mma16816<MmaT>(sd[1], qa[ks], b2, b3);
+          } else {
+            mma16816<MmaT>(sc[0], qa[ks], b0, b1);
+            mma16816<MmaT>(sc[1], qa[ks], b2, b3);
+          }
         }
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) sc[nt][e] += sd[nt][e];
       } else {
         uint32_t kw[2][8];
 #pragma unroll
@@ -512,10 +527,10 @@ int64_t env_int(const char* name, int64_t dflt) {
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
-template <typename KvT, typename ScaleT, int D, int NWM, int NWK>
+template <typename KvT, typename ScaleT, int D, int NWM, int NWK, int NS_ = 0>
 int launch_cfg(const PagedArgs& a, const MmaPlan& plan, void* ws, cudaStream_t s) {
-  using C = Cfg<KvT, D, NWM, NWK>;
-  auto kern = paged_mma_kernel<KvT, ScaleT, D, NWM, NWK>;
+  using C = Cfg<KvT, D, NWM, NWK, NS_>;
+  auto kern = paged_mma_kernel<KvT, ScaleT, D, NWM, NWK, NS_>;
   {
     static std::mutex mu;
     static uint64_t done_mask = 0;
@@ -579,12 +594,44 @@ int launch_cfg(const PagedArgs& a, const MmaPlan& plan, void* ws, cudaStream_t s
   return check_cuda(cudaGetLastError(), "paged_attention: tensor-core kernel launch");
 }
 
+// Kernel variants (consumer warps along keys NWK, stage depth NS) per shape class.
+// Fewer warps and stages per CTA let more CTAs -- and more independent TMA
+// producers -- share an SM, which keeps more page loads in flight: on B200 the
+// 16-bit decode reached 98% of measured HBM bandwidth with 2 consumer warps and 6
+// stages (4 CTAs per SM) against 64% with 4 warps and 8 stages (2 CTAs per SM).
+// NVM_ATTN_DECODE_CFG selects another variant (for sweeps).
+template <typename KvT, typename ScaleT, int D>
+int launch_decode(const PagedArgs& a, const MmaPlan& plan, void* ws, cudaStream_t s) {
+  switch (plan.variant) {
+    case 0: return launch_cfg<KvT, ScaleT, D, 1, 4>(a, plan, ws, s);
+    case 1: return launch_cfg<KvT, ScaleT, D, 1, 4, 12>(a, plan, ws, s);
+    case 3: return launch_cfg<KvT, ScaleT, D, 1, 2, 6>(a, plan, ws, s);
+    case 4: return launch_cfg<KvT, ScaleT, D, 1, 2, 8>(a, plan, ws, s);
+    case 6: return launch_cfg<KvT, ScaleT, D, 1, 1, 4>(a, plan, ws, s);
+    case 7: return launch_cfg<KvT, ScaleT, D, 1, 2, 4>(a, plan, ws, s);
+    case 8: return launch_cfg<KvT, ScaleT, D, 1, 1, 6>(a, plan, ws, s);
+    default: return launch_cfg<KvT, ScaleT, D, 1, 2, 6>(a, plan, ws, s);
+  }
+}
+
+// Three 16-row m-tiles (e.g. 8 q heads x 5 verify tokens = 40 rows).
+template <typename KvT, typename ScaleT, int D>
+int launch_m3(const PagedArgs& a, const MmaPlan& plan, void* ws, cudaStream_t s) {
+  switch (plan.variant) {
+    case 0: return launch_cfg<KvT, ScaleT, D, 3, 2>(a, plan, ws, s);
+    case 1: return launch_cfg<KvT, ScaleT, D, 3, 1, 4>(a, plan, ws, s);
+    case 2: return launch_cfg<KvT, ScaleT, D, 3, 1, 6>(a, plan, ws, s);
+    case 3: return launch_cfg<KvT, ScaleT, D, 3, 2, 6>(a, plan, ws, s);
+    default: return launch_cfg<KvT, ScaleT, D, 3, 1, 4>(a, plan, ws, s);
+  }
+}
+
 template <typename KvT, typename ScaleT, int D>
 int launch_d(const PagedArgs& a, const MmaPlan& plan, void* ws, cudaStream_t s) {
   switch (plan.nwm) {
-    case 1: return launch_cfg<KvT, ScaleT, D, 1, 4>(a, plan, ws, s);
+    case 1: return launch_decode<KvT, ScaleT, D>(a, plan, ws, s);
     case 2: return launch_cfg<KvT, ScaleT, D, 2, 2>(a, plan, ws, s);
-    case 3: return launch_cfg<KvT, ScaleT, D, 3, 2>(a, plan, ws, s);
+    case 3: return launch_m3<KvT, ScaleT, D>(a, plan, ws, s);
     default: return launch_cfg<KvT, ScaleT, D, 4, 1>(a, plan, ws, s);
   }
 }
@@ -607,6 +654,19 @@ MmaPlan plan_paged_mma(const PagedArgs& a) {
   const int64_t M = (a.Hq / a.Hkv) * a.L;
   plan.nwm = M <= 16 ? 1 : (M <= 32 ? 2 : (M <= 48 ? 3 : 4));
   plan.nwk = plan.nwm == 1 ? 4 : (plan.nwm == 4 ? 1 : 2);
+  // variant -> consumer warps along keys (must match launch_decode / launch_m3)
+  plan.variant = -1;
+  if (plan.nwm == 1) {
+    static const int kWarps1[9] = {4, 4, 2, 2, 2, 2, 1, 2, 1};
+    plan.variant = (int)env_int("NVM_ATTN_DECODE_CFG", kDefaultDecodeVariant);
+    if (plan.variant < 0 || plan.variant > 8 || plan.variant == 2 || plan.variant == 5) plan.variant = 3;
+    plan.nwk = kWarps1[plan.variant];
+  } else if (plan.nwm == 3) {
+    static const int kWarps3[4] = {2, 1, 1, 2};
+    plan.variant = (int)env_int("NVM_ATTN_M3_CFG", kDefaultM3Variant);
+    if (plan.variant < 0 || plan.variant > 3) plan.variant = 1;
+    plan.nwk = kWarps3[plan.variant];
+  }
   plan.rows_per_block = 16 * plan.nwm;
   plan.n_row_blocks = (M + plan.rows_per_block - 1) / plan.rows_per_block;
   plan.rows_real = M < plan.rows_per_block ? M : plan.rows_per_block;

@@ -116,6 +116,27 @@ size_t nvm_paged_attention_workspace_size(int64_t B, int64_t Hq, int64_t Hkv, in
                                           int64_t D, int64_t page_size, int64_t max_pages,
                                           int kv_dtype);
 
+/*
+ * nvm_paged_attention without a workspace argument.  No counterpart in the
+ * reference: it exists for callers that cannot allocate device memory on their
+ * hot path (an engine that gives all free HBM to its page pools up front, a decode
+ * loop that cannot afford cudaMalloc's implicit device synchronisation, a host
+ * without a device allocator).  Arguments and results are those of
+ * nvm_paged_attention.  The split-K scratch is a 32 MiB array built into the
+ * library, reserved on every GPU that loads the library until the process exits;
+ * sizes whose plan needs more return NVM_ERR_WORKSPACE before any GPU work.  The
+ * first call on each device resolves the array's device address (make it before
+ * any stream capture).  Every call clears the scratch tickets on `stream` and
+ * shares the one array: calls that overlap on the GPU race.  Allocates nothing.
+ */
+int nvm_paged_attention_noalloc(const void* q, int q_dtype, const void* k_pages,
+                                const void* v_pages, int kv_dtype, const void* k_scales,
+                                const void* v_scales, int scale_dtype, const int32_t* block_table,
+                                const int32_t* context_lens, void* out, int out_dtype, int64_t B,
+                                int64_t Hq, int64_t Hkv, int64_t L, int64_t D, int64_t P,
+                                int64_t page_size, int64_t max_pages, float scale, int is_causal,
+                                void* stream);
+
 /* ------------------------------------------------------------------------- */
 /* Dense flash attention (prefill)                                            */
 /* ------------------------------------------------------------------------- */

@@ -39,6 +39,8 @@ SIGNATURES = {
     "nvm_paged_attention": (_I, [_P, _I, _P, _P, _I, _P, _P, _I, _P, _P, _P, _I, _I64, _I64, _I64, _I64, _I64,
                                  _I64, _I64, _I64, _F, _I, _P, _SZ, _P]),
     "nvm_paged_attention_workspace_size": (_SZ, [_I64, _I64, _I64, _I64, _I64, _I64, _I64, _I]),
+    "nvm_paged_attention_noalloc": (_I, [_P, _I, _P, _P, _I, _P, _P, _I, _P, _P, _P, _I, _I64, _I64, _I64, _I64,
+                                         _I64, _I64, _I64, _I64, _F, _I, _P]),
     "nvm_flash_attention": (_I, [_P, _P, _P, _I, _P, _I64, _I64, _I64, _P, _I, _I64, _I64, _I64, _I64, _I64,
                                  _I64, _F, _I, _P]),
     "nvm_reshape_and_cache": (_I, [_P, _P, _I, _I64, _I64, _P, _P, _I, _P, _P, _I, _P, _I64, _I64, _I64, _I64,

@@ -35,15 +35,16 @@ namespace {
 
 constexpr int kD = 128;          // head dim
 constexpr int kBM = 128;         // query rows per CTA
-constexpr int kBN = 128;         // keys per tile
+constexpr int kBN = 64;          // keys per tile
 constexpr int kStages = 2;       // K/V ring depth
-constexpr int kTileBytes = kBN * kD * 2;  // 32 KB per K (or V) tile
+constexpr int kTileBytes = kBN * kD * 2;  // 16 KB per K (or V) tile
 constexpr int kQBytes = kBM * kD * 2;     // 32 KB
-constexpr int kPBytes = kBM * kBN * 2;    // 32 KB
 constexpr int kThreads = 192;
-constexpr int kTmemCols = 512;
-// two P buffers: bf16 P is split into hi + lo halves (see the softmax warps)
-constexpr int kSmemBytes = 1024 + kQBytes + kStages * 2 * kTileBytes + 2 * kPBytes + 256;
+constexpr int kTmemCols = 256;   // S0 [0,64), S1 [64,128), O [128,256): two CTAs fit per SM
+constexpr int kSmemBytes = 1024 + kQBytes + kStages * 2 * kTileBytes + 256;  // ~100 KB: two CTAs per SM
+// bf16 P is split into hi + lo operands only for row tiles whose rows see fewer keys
+// than this (few-key rows are where one bf16 P rounding shows in the output).
+constexpr int64_t kSplitBelowKeys = 256;
 constexpr float kRescaleThreshold = 8.0f;  // log2(256)
 
 struct Sm100Params {
@@ -57,7 +58,8 @@ struct Sm100Params {
   float scale_log2;
   int causal;
   int dense;
-  int box_rows;   // rows of one K/V TMA box: 16 (pages) or 128 (dense)
+  int box_rows;   // rows of one K/V TMA box: 16 (pages) or kBN (dense)
+  int64_t split_below;  // split bf16 P into hi + lo when the tile's first row sees fewer keys
 };
 
 __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
@@ -69,9 +71,9 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint3
 // kind::f16 instruction descriptor: f32 accumulator, A/B format, K-major A, B major
 // as given, N >> 3 at [17,23), M >> 4 at [24,29).
 template <typename T>
-__device__ __forceinline__ uint32_t idesc(bool b_mn_major) {
+__device__ __forceinline__ uint32_t idesc(bool b_mn_major, int n) {
   const uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
-  return (1u << 4) | (fmt << 7) | (fmt << 10) | ((b_mn_major ? 1u : 0u) << 16) | ((uint32_t)(kBN >> 3) << 17) |
+  return (1u << 4) | (fmt << 7) | (fmt << 10) | ((b_mn_major ? 1u : 0u) << 16) | ((uint32_t)(n >> 3) << 17) |
          ((uint32_t)(kBM >> 4) << 24);
 }
 
@@ -126,25 +128,45 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+
+// A operand from tensor memory (P), B from shared memory (V).
+__device__ __forceinline__ void mma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t db, uint32_t id, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(db), "r"(id), "r"(acc)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]),
+      "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]),
+      "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
 template <typename T>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
     flash_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                        const __grid_constant__ CUtensorMap tm_v, const Sm100Params p) {
+  constexpr bool kSplit = std::is_same<T, __nv_bfloat16>::value;  // bf16 P = hi + lo
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
-  uint8_t* sKV = sQ + kQBytes;                       // stage s: K at s*64K, V at s*64K + 32K
-  uint8_t* sP = sKV + kStages * 2 * kTileBytes;
-  uint8_t* sPlo = sP + kPBytes;                      // bf16 only: p - bf16(p)
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * kPBytes);
-  constexpr bool kSplit = std::is_same<T, __nv_bfloat16>::value;
+  uint8_t* sKV = sQ + kQBytes;  // stage s: K at s*64K, V at s*64K + 32K
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + kStages * 2 * kTileBytes);
   uint64_t* q_full = bars + 0;
   uint64_t* kv_full = bars + 1;                 // [kStages]
   uint64_t* kv_empty = bars + 1 + kStages;      // [kStages]
-  uint64_t* s_full = bars + 1 + 2 * kStages;    // [2]
-  uint64_t* p_full = bars + 3 + 2 * kStages;    // 1 (count 128)
-  uint64_t* o_done = bars + 4 + 2 * kStages;    // 1: PV_j complete
-  uint64_t* mma_done = bars + 5 + 2 * kStages;  // 1: every MMA of the CTA complete (teardown)
+  uint64_t* s_full = bars + 1 + 2 * kStages;    // [2] S_j in TMEM buffer j&1
+  uint64_t* p_full = bars + 3 + 2 * kStages;    // [2] P_j written over S_j (count 128)
+  uint64_t* o_done = bars + 5 + 2 * kStages;    // PV_j complete
+  uint64_t* mma_done = bars + 6 + 2 * kStages;  // every MMA of the CTA complete (teardown)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8 + 2 * kStages);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
@@ -179,9 +201,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
-    mbar_init(&s_full[0], 1);
-    mbar_init(&s_full[1], 1);
-    mbar_init(p_full, 128);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 128);
+    }
     mbar_init(o_done, 1);
     mbar_init(mma_done, 1);
     *abort_flag = 0;
@@ -197,8 +220,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS[2] = {tmem, tmem + 128};
-  const uint32_t tO = tmem + 256;
+  const uint32_t tO = tmem + 2 * kBN;
+  int64_t min_keys = p.causal ? (l0 + ctx - p.L + 1) : ctx_limit;  // keys seen by the tile's first row
+  const bool split = kSplit && min_keys < p.split_below;
 
   if (warp == 4) {
     // ---------------------------------------------------------------- producer
@@ -217,7 +241,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int s = j % kStages;
         bool ok = true;
         if (j >= kStages) ok = mbar_wait(&kv_empty[s], ((j / kStages) & 1) ^ 1);
-        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+        ok = __all_sync(0xffffffffu, ok) != 0;
         if (!ok || *(volatile int*)abort_flag) {
           if (lane == 0) {
             record_error(p.err, kDevErrEmptyWait);
@@ -229,7 +253,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         uint8_t* sk = sKV + s * 2 * kTileBytes;
         uint8_t* sv = sk + kTileBytes;
-        // lanes issue the boxes of this tile: (half, box) pairs for K and V
         for (int t = lane; t < 2 * boxes; t += 32) {
           const int half = t / boxes, bx = t % boxes;
           const int64_t tok0 = (int64_t)j * kBN + (int64_t)bx * p.box_rows;
@@ -250,8 +273,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         issued = j + 1;
       }
-      // drain: every issued load must land before the CTA may exit
-      if (lane == 0) {
+      if (lane == 0) {  // drain: every issued load lands before the CTA may exit
         if (!mbar_wait(q_full, 0)) record_error(p.err, kDevErrDrainWait);
         for (int s = 0; s < kStages && s < issued; ++s) {
           const int last = s + ((issued - 1 - s) / kStages) * kStages;
@@ -262,9 +284,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 5) {
     // ---------------------------------------------------------------- MMA issuer
     if (n_tiles > 0 && lane == 0) {
-      const uint32_t id_qk = idesc<T>(false);
-      const uint32_t id_pv = idesc<T>(true);
-      const uint32_t q_addr = smem_u32(sQ), p_addr = smem_u32(sP), plo_addr = smem_u32(sPlo);
+      const uint32_t id_qk = idesc<T>(false, kBN);
+      const uint32_t id_pv = idesc<T>(true, kD);
+      const uint32_t q_addr = smem_u32(sQ);
       bool ok = mbar_wait(q_full, 0);
       auto issue_s = [&](int j) -> bool {
         const int s = j % kStages;
@@ -273,10 +295,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t k_addr = smem_u32(sKV + s * 2 * kTileBytes);
 #pragma unroll
         for (int ks = 0; ks < kD / 16; ++ks) {
-          const uint32_t koff = (uint32_t)((ks >> 2) * (kBM * 128) + (ks & 3) * 32);
-          const uint64_t da = smem_desc(q_addr + koff, 16, 1024);
+          const uint64_t da = smem_desc(q_addr + (uint32_t)((ks >> 2) * (kBM * 128) + (ks & 3) * 32), 16, 1024);
           const uint64_t db = smem_desc(k_addr + (uint32_t)((ks >> 2) * (kBN * 128) + (ks & 3) * 32), 16, 1024);
-          mma_f16(tS[j & 1], da, db, id_qk, ks > 0 ? 1u : 0u);
+          mma_f16(tmem + (uint32_t)((j & 1) * kBN), da, db, id_qk, ks > 0 ? 1u : 0u);
         }
         mma_commit(&s_full[j & 1]);
         return true;
@@ -284,31 +305,39 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ok) ok = issue_s(0);
       if (ok && n_tiles > 1) ok = issue_s(1);
       for (int j = 0; ok && j < n_tiles; ++j) {
-        // P_j written by the softmax warps (which also finished reading S_j)
-        if (!mbar_wait(p_full, j & 1)) {
+        // P_j (over S_j's TMEM columns) written by the softmax warps
+        if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const int s = j % kStages;
         const uint32_t v_addr = smem_u32(sKV + s * 2 * kTileBytes + kTileBytes);
+        const uint32_t tp = tmem + (uint32_t)((j & 1) * kBN);
 #pragma unroll
         for (int ks = 0; ks < kBN / 16; ++ks) {
-          const uint32_t poff = (uint32_t)((ks >> 2) * (kBM * 128) + (ks & 3) * 32);
           // V is MN-major: 64-column halves kBN*128 bytes apart (LBO), 8-token groups 1024 apart (SBO)
           const uint64_t db = smem_desc(v_addr + (uint32_t)(ks * 16 * 128), kBN * 128, 1024);
-          mma_f16(tO, smem_desc(p_addr + poff, 16, 1024), db, id_pv, (j > 0 || ks > 0) ? 1u : 0u);
-          if (kSplit) mma_f16(tO, smem_desc(plo_addr + poff, 16, 1024), db, id_pv, 1u);
+          mma_f16_ts(tO, tp + (uint32_t)(ks * 8), db, id_pv, (j > 0 || ks > 0) ? 1u : 0u);
+          if (split) mma_f16_ts(tO, tp + (uint32_t)(kBN / 2 + ks * 8), db, id_pv, 1u);
         }
         mma_commit(o_done);
         mma_commit(&kv_empty[s]);
-        if (j + 2 < n_tiles) ok = issue_s(j + 2);
+        // S_{j+2} reuses S_j's TMEM columns, which hold P_j: wait until PV_j has
+        // finished reading them (o_done phase j) before overwriting.
+        if (j + 2 < n_tiles) {
+          if (!mbar_wait(o_done, j & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          ok = issue_s(j + 2);
+        }
       }
       if (!ok) {
         record_error(p.err, kDevErrMmaWait);
         *(volatile int*)abort_flag = 1;
       }
-      // arrives once every MMA issued by this thread has finished (TMEM teardown)
       mma_commit(mma_done);
     }
   } else {
@@ -326,9 +355,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
+      const uint32_t tS = tmem + lane_base + (uint32_t)((j & 1) * kBN);
       float sv[kBN];
 #pragma unroll
-      for (int c = 0; c < kBN / 32; ++c) tmem_ld32(tS[j & 1] + lane_base + c * 32, *reinterpret_cast<float(*)[32]>(&sv[c * 32]));
+      for (int c = 0; c < kBN / 32; ++c) tmem_ld32(tS + c * 32, *reinterpret_cast<float(*)[32]>(&sv[c * 32]));
       tmem_wait_ld();
       const int64_t key0 = (int64_t)j * kBN;
       const bool need_mask = key0 + kBN > clean || !row_ok;
@@ -341,10 +371,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (key >= ctx_limit || key > lim) x = -INFINITY;
         }
         sv[c] = x;
-        mx = fmaxf(mx, x);
       }
-      // holes: whole 16-token groups of missing pages are masked
-      if (!p.dense) {
+      if (!p.dense) {  // holes: the 16-token groups of missing pages are masked
 #pragma unroll
         for (int g = 0; g < kBN / 16; ++g) {
           const int64_t pidx = (key0 + g * 16) / p.ps;
@@ -354,10 +382,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int c = 0; c < 16; ++c) sv[g * 16 + c] = -INFINITY;
           }
         }
-        mx = -INFINITY;
-#pragma unroll
-        for (int c = 0; c < kBN; ++c) mx = fmaxf(mx, sv[c]);
       }
+#pragma unroll
+      for (int c = 0; c < kBN; ++c) mx = fmaxf(mx, sv[c]);
       // lazy max: keep the old reference max unless the new one exceeds it by > 8
       float m_ref = m;
       bool rescale = false;
@@ -375,60 +402,60 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       lsum = (m == -INFINITY ? 0.f : lsum * alpha) + rs;
       m = m_ref;
-      // wait until PV_{j-1} finished: P buffers free, O stable for rescaling
-      if (j > 0) {
+      if (__any_sync(0xffffffffu, rescale)) {
+        // O must hold PV_{j-1} before it is rescaled
         if (!warp_wait(o_done, (j - 1) & 1)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        if (__any_sync(0xffffffffu, rescale)) {
-          const float f = rescale ? alpha : 1.f;
+        const float f = rescale ? alpha : 1.f;
 #pragma unroll 1
-          for (int c = 0; c < kD / 32; ++c) {
-            float ov[32];
-            tmem_ld32(tO + lane_base + c * 32, ov);
-            tmem_wait_ld();
+        for (int c = 0; c < kD / 32; ++c) {
+          float ov[32];
+          tmem_ld32(tO + lane_base + c * 32, ov);
+          tmem_wait_ld();
 #pragma unroll
-            for (int x = 0; x < 32; ++x) ov[x] *= f;
-            tmem_st32(tO + lane_base + c * 32, ov);
-          }
-          tmem_wait_st();
+          for (int x = 0; x < 32; ++x) ov[x] *= f;
+          tmem_st32(tO + lane_base + c * 32, ov);
         }
       }
-      // P row -> shared memory, 128B-swizzled K-major: atom a = key/64, chunk c = (key%64)/8
-      const int rswz = row & 7;
+      // P over S_j's columns: packed pairs, hi in columns [0, kBN/2), lo (bf16 split) after
+      {
+        uint32_t hi[32];
 #pragma unroll
-      for (int ch = 0; ch < kBN / 8; ++ch) {
-        const int a = ch >> 3, c = ch & 7;
-        const uint32_t off = (uint32_t)(a * (kBM * 128) + row * 128 + ((c ^ rswz) << 4));
-        uint32_t hi[4];
+        for (int x = 0; x < 32; ++x) hi[x] = pack2<T>(sv[2 * x], sv[2 * x + 1]);
+        tmem_st32u(tS, hi);
+        if (split) {
+          uint32_t lo[32];
 #pragma unroll
-        for (int x = 0; x < 4; ++x) hi[x] = pack2<T>(sv[ch * 8 + 2 * x], sv[ch * 8 + 2 * x + 1]);
-        *reinterpret_cast<uint4*>(sP + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-        if constexpr (kSplit) {
-          uint32_t lo[4];
-#pragma unroll
-          for (int x = 0; x < 4; ++x) {
-            const __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&hi[x]);
-            lo[x] = pack2<T>(sv[ch * 8 + 2 * x] - __low2float(h), sv[ch * 8 + 2 * x + 1] - __high2float(h));
+          for (int x = 0; x < 32; ++x) {
+            const __nv_bfloat162 hh = *reinterpret_cast<const __nv_bfloat162*>(&hi[x]);
+            lo[x] = pack2<T>(sv[2 * x] - __low2float(hh), sv[2 * x + 1] - __high2float(hh));
           }
-          *reinterpret_cast<uint4*>(sPlo + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+          tmem_st32u(tS + kBN / 2, lo);
         }
       }
-      fence_async_smem();
+      tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[j & 1]);
     }
-    // final O: wait for the last PV, normalise, store
-    if (ok && n_tiles > 0 && !warp_wait(o_done, (n_tiles - 1) & 1)) ok = false;
+    // final O: wait for the last PV, normalise, stage through shared memory, store coalesced.
+    // The wait is on mma_done (one completion per CTA), not on o_done: a parity wait
+    // only tells "phase k done" from "phase k+1 done", and these warps may arrive here
+    // while PV_{n-2} is still running, when o_done's parity already matches PV_{n-1}'s.
+    if (ok && n_tiles > 0 && !warp_wait(mma_done, 0)) ok = false;
     if (!ok) {
       record_error(p.err, kDevErrFullWait);
       *(volatile int*)abort_flag = 1;
     }
     tc_fence_after();
     const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
-    const int64_t orow = (n * p.L + lrow) * kD;
+    const int esz = p.out_dtype == NVM_F32 ? 4 : 2;
+    const int row_bytes = kD * esz;               // 256 or 512
+    const int chunks = row_bytes / 16;            // 16-byte chunks per row
+    uint8_t* stage = sKV;                         // K/V ring is free once every PV is done
+    uint8_t* srow = stage + row * row_bytes;
 #pragma unroll 1
     for (int c = 0; c < kD / 32; ++c) {
       float ov[32];
@@ -439,10 +466,39 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int x = 0; x < 32; ++x) ov[x] = 0.f;
       }
-      if (row_ok) {
+      // 32 values = 8 (fp32) or 4 (16-bit) chunks of 16 bytes, chunk index XOR row%8
 #pragma unroll
-        for (int x = 0; x < 32; ++x) store_dyn(p.out, orow + c * 32 + x, p.out_dtype, ov[x] * inv);
+      for (int x = 0; x < 32; x += (16 / 4)) {
+        if (esz == 4) {
+          const int ch = (c * 32 + x) / 4;
+          *reinterpret_cast<float4*>(srow + ((ch ^ (row & 7)) << 4)) =
+              make_float4(ov[x] * inv, ov[x + 1] * inv, ov[x + 2] * inv, ov[x + 3] * inv);
+        }
       }
+      if (esz == 2) {
+#pragma unroll
+        for (int x = 0; x < 32; x += 8) {
+          const int ch = (c * 32 + x) / 8;
+          uint4 v4;
+          if (p.out_dtype == NVM_BF16) {
+            v4 = make_uint4(pack2<__nv_bfloat16>(ov[x] * inv, ov[x + 1] * inv),
+                            pack2<__nv_bfloat16>(ov[x + 2] * inv, ov[x + 3] * inv),
+                            pack2<__nv_bfloat16>(ov[x + 4] * inv, ov[x + 5] * inv),
+                            pack2<__nv_bfloat16>(ov[x + 6] * inv, ov[x + 7] * inv));
+          } else {
+            v4 = make_uint4(pack2<__half>(ov[x] * inv, ov[x + 1] * inv), pack2<__half>(ov[x + 2] * inv, ov[x + 3] * inv),
+                            pack2<__half>(ov[x + 4] * inv, ov[x + 5] * inv), pack2<__half>(ov[x + 6] * inv, ov[x + 7] * inv));
+          }
+          *reinterpret_cast<uint4*>(srow + ((ch ^ (row & 7)) << 4)) = v4;
+        }
+      }
+    }
+    named_barrier(1, 128);
+    uint8_t* gout = reinterpret_cast<uint8_t*>(p.out) + (n * p.L + l0) * (int64_t)row_bytes;
+    for (int idx = row; idx < (int)rows * chunks; idx += 128) {
+      const int r = idx / chunks, ch = idx % chunks;
+      *reinterpret_cast<uint4*>(gout + (int64_t)r * row_bytes + ch * 16) =
+          *reinterpret_cast<const uint4*>(stage + r * row_bytes + ((ch ^ (r & 7)) << 4));
     }
   }
 
@@ -458,7 +514,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// One opt-in to the 225 KB dynamic shared memory per kernel instantiation and device.
+// One opt-in to the dynamic shared memory size per kernel instantiation and device.
 template <typename T>
 int launch_typed(dim3 grid, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                  const Sm100Params& p, cudaStream_t s) {
@@ -488,7 +544,7 @@ bool sm100_prefill_eligible(const PagedArgs& a) {
   if (a.D != kD) return false;
   if (a.L < 64) return false;
   if (a.dense) {
-    if (a.page_size < kBN) return false;  // dense boxes are 128 rows
+    if (a.page_size < kBN) return false;  // dense boxes are kBN rows
   } else if (a.page_size != 16) {
     return false;
   }
@@ -507,7 +563,7 @@ int launch_sm100_prefill(const PagedArgs& a, cudaStream_t s) {
   int st = encode_tmap(&tq, dt, 3, a.q, qd, qs, qb, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != NVM_OK) return st;
   // pools [P, Hkv, ps, D] -> (D, ps, Hkv, P)
-  const int box_rows = a.dense ? kBN : 16;
+  const int box_rows = a.dense ? kBN : 16;  // dense: one box per 64-key half tile
   const uint64_t kd[4] = {(uint64_t)kD, (uint64_t)a.page_size, (uint64_t)a.Hkv, (uint64_t)a.P};
   const uint64_t ks[3] = {kD * 2, (uint64_t)a.page_size * kD * 2, (uint64_t)(a.Hkv * a.page_size) * kD * 2};
   const uint32_t kb[4] = {64u, (uint32_t)box_rows, 1u, 1u};
@@ -524,6 +580,10 @@ int launch_sm100_prefill(const PagedArgs& a, cudaStream_t s) {
   p.n_row_tiles = (a.L + kBM - 1) / kBM;
   p.scale_log2 = a.scale * 1.4426950408889634f;
   p.causal = a.is_causal; p.dense = a.dense; p.box_rows = box_rows;
+  {
+    const char* e = std::getenv("NVM_SM100_SPLIT_BELOW");  // tuning: 0 = never split, huge = always
+    p.split_below = (e != nullptr && e[0] != '\0') ? std::atoll(e) : kSplitBelowKeys;
+  }
 
   const dim3 grid((unsigned)(a.B * a.Hq * p.n_row_tiles));
   if (a.kv_dtype == NVM_F16) return launch_typed<__half>(grid, tq, tk, tv, p, s);

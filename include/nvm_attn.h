@@ -71,7 +71,10 @@ const char* nvm_version(void);
  * iteration/time limit; when one expires the kernel records a nonzero code here,
  * drains its own in-flight copies (bounded) and returns, leaving the context
  * usable.  nvm_device_error() synchronises `stream`, reads the word of the current
- * device, optionally clears it, and returns it (0 = no error).
+ * device, optionally clears it, and returns it (0 = no error).  The first code
+ * recorded stays: 1 a wait for a tile to land expired, 2 a wait for a free stage,
+ * 3 draining in-flight copies, 4 tensor-memory allocation, 5 tensor-core completion,
+ * 6 dynamic shared memory was not 1024-byte aligned (that kernel computed nothing).
  */
 int nvm_device_error(void* stream, int clear);
 

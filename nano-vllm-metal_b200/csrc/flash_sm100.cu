@@ -7,19 +7,21 @@
 // the multi-query paged kernel paged_attention_kv (paged_attention.metal:6-128);
 // same semantics (causal key limit row + ctx - L, holes skipped, empty rows zero).
 //
-// One CTA computes a 128-row query tile of one q head:
-//   warps 0-3  softmax: thread i owns query row i = TMEM lane i.  Reads S rows with
-//              tcgen05.ld, keeps the running max / sum in registers, writes P (bf16/
-//              f16) into shared memory in the 128B-swizzled K-major layout the tensor
-//              core reads, rescales the O accumulator in TMEM only when the row max
-//              grew by more than 2^8 (the stale max keeps every p <= 256).
-//   warp 4     producer: TMA loads of the Q tile and of 128-token K/V tiles (pages
-//              of 16 tokens for paged context, 128-row boxes for dense) into a
-//              two-stage ring; holes load an out-of-range page (zero fill).
-//   warp 5     MMA issuer: allocates 512 TMEM columns (S double buffer + O), issues
-//              S = Q K^T and O += P V as tcgen05.mma kind::f16 (M=128, N=128, fp32
-//              accumulate) from one thread, and signals completion with
-//              tcgen05.commit on mbarriers.
+// One CTA computes a 128-row query tile of one q head (two CTAs per SM):
+//   warps 0-3  softmax: thread i owns query row i = TMEM lane i.  Reads a 64-key S
+//              row slice with tcgen05.ld, keeps the running max / sum in registers,
+//              writes P (bf16/f16 pairs; bf16 as hi + lo for rows that see few keys)
+//              back over S's TMEM columns with tcgen05.st, and rescales the O
+//              accumulator in TMEM only when the row max grew by more than 2^8 (the
+//              stale max keeps every p <= 256).  Masking costs one compare per score
+//              and only in tiles that cross a row's last visible key.
+//   warp 4     producer: TMA loads of the Q tile and of 64-token K and V tiles (pages
+//              of 16 tokens for paged context, 64-row boxes for dense) into a 3-stage K
+//              ring and a 2-stage V ring; holes load an out-of-range page (zero fill).
+//   warp 5     MMA issuer: allocates 256 TMEM columns (S double buffer + O), issues
+//              S = Q K^T (N=64) and O += P V (A = P from TMEM, N=128) as tcgen05.mma
+//              kind::f16 with fp32 accumulate from one thread, and signals completion
+//              with tcgen05.commit on mbarriers.
 // Every mbarrier wait is bounded; on expiry the CTA records an error, lets its own
 // copies and MMAs land (bounded), frees TMEM and returns.
 #include <type_traits>
@@ -36,12 +38,15 @@ namespace {
 constexpr int kD = 128;          // head dim
 constexpr int kBM = 128;         // query rows per CTA
 constexpr int kBN = 64;          // keys per tile
-constexpr int kStages = 2;       // K/V ring depth
+constexpr int kKStages = 3;      // K ring: a K stage frees as soon as S_j = Q K_j^T is done
+constexpr int kVStages = 2;      // V ring: a V stage frees when PV_j is done
 constexpr int kTileBytes = kBN * kD * 2;  // 16 KB per K (or V) tile
 constexpr int kQBytes = kBM * kD * 2;     // 32 KB
+constexpr int kRingBytes = (kKStages + kVStages) * kTileBytes;  // 80 KB, also the epilogue's staging area
 constexpr int kThreads = 192;
 constexpr int kTmemCols = 256;   // S0 [0,64), S1 [64,128), O [128,256): two CTAs fit per SM
-constexpr int kSmemBytes = 1024 + kQBytes + kStages * 2 * kTileBytes + 256;  // ~100 KB: two CTAs per SM
+constexpr int kSmemBytes = kQBytes + kRingBytes + 256;  // 112.25 KB (+1 KB reserved each): two CTAs per SM
+static_assert(kRingBytes >= kBM * kD * 4, "the epilogue stages a 128 x 128 fp32 tile in the K/V ring");
 // bf16 P is split into hi + lo operands only for row tiles whose rows see fewer keys
 // than this (few-key rows are where one bf16 P rounding shows in the output).
 constexpr int64_t kSplitBelowKeys = 256;
@@ -93,7 +98,6 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   uint32_t* r = reinterpret_cast<uint32_t*>(v);
@@ -123,6 +127,13 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
   const bool ok = mbar_wait(bar, parity);
   return __all_sync(0xffffffffu, ok) != 0;
+}
+
+// 2^x on the MUFU unit (PTX ex2.approx.ftz.f32): -inf gives +0, subnormal results flush to 0.
+__device__ __forceinline__ float ex2_ftz(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
@@ -155,19 +166,25 @@ __global__ void __launch_bounds__(kThreads, 2)
     flash_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                        const __grid_constant__ CUtensorMap tm_v, const Sm100Params p) {
   constexpr bool kSplit = std::is_same<T, __nv_bfloat16>::value;  // bf16 P = hi + lo
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  extern __shared__ __align__(1024) uint8_t smem[];
+  if ((smem_u32(smem) & 1023u) != 0) {  // 128B-swizzled tiles need a 1024-byte aligned base
+    if (threadIdx.x == 0) record_error(p.err, kDevErrSmemAlign);
+    return;
+  }
   uint8_t* sQ = smem;
-  uint8_t* sKV = sQ + kQBytes;  // stage s: K at s*64K, V at s*64K + 32K
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + kStages * 2 * kTileBytes);
-  uint64_t* q_full = bars + 0;
-  uint64_t* kv_full = bars + 1;                 // [kStages]
-  uint64_t* kv_empty = bars + 1 + kStages;      // [kStages]
-  uint64_t* s_full = bars + 1 + 2 * kStages;    // [2] S_j in TMEM buffer j&1
-  uint64_t* p_full = bars + 3 + 2 * kStages;    // [2] P_j written over S_j (count 128)
-  uint64_t* o_done = bars + 5 + 2 * kStages;    // PV_j complete
-  uint64_t* mma_done = bars + 6 + 2 * kStages;  // every MMA of the CTA complete (teardown)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8 + 2 * kStages);
+  uint8_t* sK = smem + kQBytes;             // [kKStages] K tiles
+  uint8_t* sV = sK + kKStages * kTileBytes;  // [kVStages] V tiles
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sK + kRingBytes);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = q_full + 1;             // [kKStages] K_j landed
+  uint64_t* k_empty = k_full + kKStages;     // [kKStages] S_j has read K_j
+  uint64_t* v_full = k_empty + kKStages;     // [kVStages] V_j landed
+  uint64_t* v_empty = v_full + kVStages;     // [kVStages] PV_j has read V_j
+  uint64_t* s_full = v_empty + kVStages;     // [2] S_j in TMEM buffer j&1
+  uint64_t* p_full = s_full + 2;             // [2] P_j written over S_j (count 128)
+  uint64_t* o_done = p_full + 2;             // PV_j complete
+  uint64_t* mma_done = o_done + 1;           // every MMA of the CTA complete (one completion)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -188,18 +205,16 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
   if (ctx <= 0 || need < 0) need = 0;
   const int n_tiles = (int)((need + kBN - 1) / kBN);
-  // keys below `clean` are visible to every row of the tile
-  int64_t clean = ctx_limit;
-  if (p.causal) {
-    const int64_t lim0 = l0 + ctx - p.L + 1;
-    if (lim0 < clean) clean = lim0;
-  }
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+    for (int s = 0; s < kKStages; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+    }
+    for (int s = 0; s < kVStages; ++s) {
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
@@ -226,7 +241,8 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   if (warp == 4) {
     // ---------------------------------------------------------------- producer
-    int issued = 0;
+    // Loads run in the order the MMA warp consumes them: K_0, K_1, V_0, K_2, V_1, ...
+    int k_issued = 0, v_issued = 0;
     if (n_tiles > 0) {
       if (lane == 0) {
         prefetch_tmap(&tm_q);
@@ -237,22 +253,24 @@ __global__ void __launch_bounds__(kThreads, 2)
         tma_load_3d(sQ + kBM * 128, &tm_q, 64, (int)l0, (int)n, q_full);
       }
       const int boxes = kBN / p.box_rows;  // K/V boxes per 64-column half
-      for (int j = 0; j < n_tiles; ++j) {
-        const int s = j % kStages;
+      auto load_tile = [&](bool is_k, int j) -> bool {
+        const int ns = is_k ? kKStages : kVStages;
+        const int s = j % ns;
+        uint64_t* full = (is_k ? k_full : v_full) + s;
         bool ok = true;
-        if (j >= kStages) ok = mbar_wait(&kv_empty[s], ((j / kStages) & 1) ^ 1);
+        if (j >= ns) ok = mbar_wait((is_k ? k_empty : v_empty) + s, ((j / ns) & 1) ^ 1);
         ok = __all_sync(0xffffffffu, ok) != 0;
         if (!ok || *(volatile int*)abort_flag) {
           if (lane == 0) {
             record_error(p.err, kDevErrEmptyWait);
             *(volatile int*)abort_flag = 1;
           }
-          break;
+          return false;
         }
-        if (lane == 0) mbar_arrive_expect_tx(&kv_full[s], 2 * kTileBytes);
+        if (lane == 0) mbar_arrive_expect_tx(full, kTileBytes);
         __syncwarp();
-        uint8_t* sk = sKV + s * 2 * kTileBytes;
-        uint8_t* sv = sk + kTileBytes;
+        uint8_t* dst = (is_k ? sK : sV) + s * kTileBytes;
+        const CUtensorMap* tm = is_k ? &tm_k : &tm_v;
         for (int t = lane; t < 2 * boxes; t += 32) {
           const int half = t / boxes, bx = t % boxes;
           const int64_t tok0 = (int64_t)j * kBN + (int64_t)bx * p.box_rows;
@@ -268,17 +286,26 @@ __global__ void __launch_bounds__(kThreads, 2)
             slot0 = (int)(tok0 % p.ps);
           }
           const uint32_t off = (uint32_t)(half * kBN * 128 + bx * p.box_rows * 128);
-          tma_load_4d(sk + off, &tm_k, half * 64, slot0, (int)kvh, pid, &kv_full[s]);
-          tma_load_4d(sv + off, &tm_v, half * 64, slot0, (int)kvh, pid, &kv_full[s]);
+          tma_load_4d(dst + off, tm, half * 64, slot0, (int)kvh, pid, full);
         }
-        issued = j + 1;
+        if (is_k) k_issued = j + 1; else v_issued = j + 1;
+        return true;
+      };
+      bool ok = true;
+      for (int t = 0; ok && t <= n_tiles; ++t) {
+        if (t < n_tiles) ok = load_tile(true, t);
+        if (ok && t >= 1) ok = load_tile(false, t - 1);
       }
       if (lane == 0) {  // drain: every issued load lands before the CTA may exit
         if (!mbar_wait(q_full, 0)) record_error(p.err, kDevErrDrainWait);
-        for (int s = 0; s < kStages && s < issued; ++s) {
-          const int last = s + ((issued - 1 - s) / kStages) * kStages;
-          if (!mbar_wait(&kv_full[s], (last / kStages) & 1)) record_error(p.err, kDevErrDrainWait);
-        }
+        auto drain = [&](uint64_t* full, int ns, int issued) {
+          for (int s = 0; s < ns && s < issued; ++s) {
+            const int last = s + ((issued - 1 - s) / ns) * ns;
+            if (!mbar_wait(&full[s], (last / ns) & 1)) record_error(p.err, kDevErrDrainWait);
+          }
+        };
+        drain(k_full, kKStages, k_issued);
+        drain(v_full, kVStages, v_issued);
       }
     }
   } else if (warp == 5) {
@@ -289,10 +316,10 @@ __global__ void __launch_bounds__(kThreads, 2)
       const uint32_t q_addr = smem_u32(sQ);
       bool ok = mbar_wait(q_full, 0);
       auto issue_s = [&](int j) -> bool {
-        const int s = j % kStages;
-        if (!mbar_wait(&kv_full[s], (j / kStages) & 1)) return false;
+        const int s = j % kKStages;
+        if (!mbar_wait(&k_full[s], (j / kKStages) & 1)) return false;
         tc_fence_after();
-        const uint32_t k_addr = smem_u32(sKV + s * 2 * kTileBytes);
+        const uint32_t k_addr = smem_u32(sK + s * kTileBytes);
 #pragma unroll
         for (int ks = 0; ks < kD / 16; ++ks) {
           const uint64_t da = smem_desc(q_addr + (uint32_t)((ks >> 2) * (kBM * 128) + (ks & 3) * 32), 16, 1024);
@@ -300,19 +327,20 @@ __global__ void __launch_bounds__(kThreads, 2)
           mma_f16(tmem + (uint32_t)((j & 1) * kBN), da, db, id_qk, ks > 0 ? 1u : 0u);
         }
         mma_commit(&s_full[j & 1]);
+        mma_commit(&k_empty[s]);
         return true;
       };
       if (ok) ok = issue_s(0);
       if (ok && n_tiles > 1) ok = issue_s(1);
       for (int j = 0; ok && j < n_tiles; ++j) {
-        // P_j (over S_j's TMEM columns) written by the softmax warps
-        if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1)) {
+        // P_j (over S_j's TMEM columns) written by the softmax warps, V_j landed
+        const int s = j % kVStages;
+        if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1) || !mbar_wait(&v_full[s], (j / kVStages) & 1)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const int s = j % kStages;
-        const uint32_t v_addr = smem_u32(sKV + s * 2 * kTileBytes + kTileBytes);
+        const uint32_t v_addr = smem_u32(sV + s * kTileBytes);
         const uint32_t tp = tmem + (uint32_t)((j & 1) * kBN);
 #pragma unroll
         for (int ks = 0; ks < kBN / 16; ++ks) {
@@ -322,7 +350,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           if (split) mma_f16_ts(tO, tp + (uint32_t)(kBN / 2 + ks * 8), db, id_pv, 1u);
         }
         mma_commit(o_done);
-        mma_commit(&kv_empty[s]);
+        mma_commit(&v_empty[s]);
         // S_{j+2} reuses S_j's TMEM columns, which hold P_j: wait until PV_j has
         // finished reading them (o_done phase j) before overwriting.
         if (j + 2 < n_tiles) {
@@ -345,9 +373,12 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int row = warp * 32 + lane;            // TMEM lane == query row in the tile
     const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
     const int64_t lrow = l0 + row;               // query index
-    const bool row_ok = row < rows;
-    const int64_t lim = p.causal ? (lrow + ctx - p.L) : INT64_MAX / 4;  // last visible key
-    float m = -INFINITY, lsum = 0.f;
+    // last key this row may see: inside the context and, when causal, key <= row + ctx - L
+    int64_t last_key = ctx_limit - 1;
+    if (p.causal && lrow + ctx - p.L < last_key) last_key = lrow + ctx - p.L;
+    if (row >= rows) last_key = -1;
+    const float sl2 = p.scale_log2;  // > 0, so max(s) * sl2 == max(s * sl2)
+    float m = -INFINITY, lsum = 0.f;  // running max (log2 units, lazily updated) and sum
     bool ok = true;
     for (int j = 0; j < n_tiles; ++j) {
       if (!warp_wait(&s_full[j & 1], (j >> 1) & 1)) {
@@ -361,16 +392,13 @@ __global__ void __launch_bounds__(kThreads, 2)
       for (int c = 0; c < kBN / 32; ++c) tmem_ld32(tS + c * 32, *reinterpret_cast<float(*)[32]>(&sv[c * 32]));
       tmem_wait_ld();
       const int64_t key0 = (int64_t)j * kBN;
-      const bool need_mask = key0 + kBN > clean || !row_ok;
-      float mx = -INFINITY;
+      // Only tiles that cross some row's last visible key (the causal diagonal, the
+      // context end, rows past L) pay for the mask: one compare per score.
+      const int64_t vis64 = last_key - key0;  // in-tile index of the row's last visible key
+      if (__any_sync(0xffffffffu, vis64 < kBN - 1)) {
+        const int vis = vis64 < -1 ? -1 : (int)vis64;
 #pragma unroll
-      for (int c = 0; c < kBN; ++c) {
-        float x = sv[c] * p.scale_log2;
-        if (need_mask) {
-          const int64_t key = key0 + c;
-          if (key >= ctx_limit || key > lim) x = -INFINITY;
-        }
-        sv[c] = x;
+        for (int c = 0; c < kBN; ++c) sv[c] = c <= vis ? sv[c] : -INFINITY;
       }
       if (!p.dense) {  // holes: the 16-token groups of missing pages are masked
 #pragma unroll
@@ -383,23 +411,32 @@ __global__ void __launch_bounds__(kThreads, 2)
           }
         }
       }
+      float mx = sv[0];
 #pragma unroll
-      for (int c = 0; c < kBN; ++c) mx = fmaxf(mx, sv[c]);
+      for (int c = 1; c < kBN; ++c) mx = fmaxf(mx, sv[c]);
+      const float mx_s = mx * sl2;
       // lazy max: keep the old reference max unless the new one exceeds it by > 8
       float m_ref = m;
       bool rescale = false;
-      if (mx > -INFINITY && (m == -INFINITY || mx > m + kRescaleThreshold)) {
+      if (mx_s > -INFINITY && (m == -INFINITY || mx_s > m + kRescaleThreshold)) {
         rescale = m != -INFINITY;
-        m_ref = mx;
+        m_ref = mx_s;
       }
       const float mu = m_ref == -INFINITY ? 0.f : m_ref;
-      const float alpha = exp2f(m - mu);  // 0 when m == -inf
-      float rs = 0.f;
+      const float alpha = ex2_ftz(m - mu);  // 0 when m == -inf
+      float r0 = 0.f, r1 = 0.f, r2 = 0.f, r3 = 0.f;
 #pragma unroll
-      for (int c = 0; c < kBN; ++c) {
-        sv[c] = exp2f(sv[c] - mu);
-        rs += sv[c];
+      for (int c = 0; c < kBN; c += 4) {
+        sv[c] = ex2_ftz(fmaf(sv[c], sl2, -mu));
+        sv[c + 1] = ex2_ftz(fmaf(sv[c + 1], sl2, -mu));
+        sv[c + 2] = ex2_ftz(fmaf(sv[c + 2], sl2, -mu));
+        sv[c + 3] = ex2_ftz(fmaf(sv[c + 3], sl2, -mu));
+        r0 += sv[c];
+        r1 += sv[c + 1];
+        r2 += sv[c + 2];
+        r3 += sv[c + 3];
       }
+      const float rs = (r0 + r1) + (r2 + r3);
       lsum = (m == -INFINITY ? 0.f : lsum * alpha) + rs;
       m = m_ref;
       if (__any_sync(0xffffffffu, rescale)) {
@@ -454,7 +491,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int esz = p.out_dtype == NVM_F32 ? 4 : 2;
     const int row_bytes = kD * esz;               // 256 or 512
     const int chunks = row_bytes / 16;            // 16-byte chunks per row
-    uint8_t* stage = sKV;                         // K/V ring is free once every PV is done
+    uint8_t* stage = sK;                          // the K/V ring is free once every MMA is done
     uint8_t* srow = stage + row * row_bytes;
 #pragma unroll 1
     for (int c = 0; c < kD / 32; ++c) {
@@ -543,6 +580,7 @@ bool sm100_prefill_eligible(const PagedArgs& a) {
   if (a.q_dtype != a.kv_dtype) return false;
   if (a.D != kD) return false;
   if (a.L < 64) return false;
+  if (!(a.scale > 0.f)) return false;  // the softmax takes row maxima before scaling
   if (a.dense) {
     if (a.page_size < kBN) return false;  // dense boxes are kBN rows
   } else if (a.page_size != 16) {

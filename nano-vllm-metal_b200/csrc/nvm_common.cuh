@@ -22,6 +22,7 @@ enum DeviceError : int {
   kDevErrDrainWait = 3,   // in-flight copies did not land while draining
   kDevErrTmemAlloc = 4,   // tensor-memory allocation wait expired
   kDevErrMmaWait = 5,     // tensor-core completion wait expired
+  kDevErrSmemAlign = 6,   // dynamic shared memory not 1024-byte aligned (kernel did nothing)
 };
 
 // Every spin-wait gives up after this many nanoseconds of %globaltimer.

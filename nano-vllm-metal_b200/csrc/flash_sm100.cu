@@ -136,6 +136,22 @@ __device__ __forceinline__ float ex2_ftz(float x) {
   return y;
 }
 
+// Round two floats to a packed 16-bit pair in one instruction: a in the low half, b in the high.
+template <typename T>
+__device__ __forceinline__ uint32_t cvt_pack(float a, float b);
+template <>
+__device__ __forceinline__ uint32_t cvt_pack<__nv_bfloat16>(float a, float b) {
+  uint32_t d;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(b), "f"(a));
+  return d;
+}
+template <>
+__device__ __forceinline__ uint32_t cvt_pack<__half>(float a, float b) {
+  uint32_t d;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(b), "f"(a));
+  return d;
+}
+
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
@@ -241,90 +257,106 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   if (warp == 4) {
     // ---------------------------------------------------------------- producer
+    // One thread, straight-line: this warp shares its scheduler with two softmax warps
+    // that issue nearly every cycle, so each instruction here costs several cycles.
     // Loads run in the order the MMA warp consumes them: K_0, K_1, V_0, K_2, V_1, ...
-    int k_issued = 0, v_issued = 0;
-    if (n_tiles > 0) {
-      if (lane == 0) {
-        prefetch_tmap(&tm_q);
-        prefetch_tmap(&tm_k);
-        prefetch_tmap(&tm_v);
-        mbar_arrive_expect_tx(q_full, kQBytes);
-        tma_load_3d(sQ, &tm_q, 0, (int)l0, (int)n, q_full);
-        tma_load_3d(sQ + kBM * 128, &tm_q, 64, (int)l0, (int)n, q_full);
-      }
-      const int boxes = kBN / p.box_rows;  // K/V boxes per 64-column half
-      auto load_tile = [&](bool is_k, int j) -> bool {
-        const int ns = is_k ? kKStages : kVStages;
-        const int s = j % ns;
-        uint64_t* full = (is_k ? k_full : v_full) + s;
-        bool ok = true;
-        if (j >= ns) ok = mbar_wait((is_k ? k_empty : v_empty) + s, ((j / ns) & 1) ^ 1);
-        ok = __all_sync(0xffffffffu, ok) != 0;
-        if (!ok || *(volatile int*)abort_flag) {
-          if (lane == 0) {
-            record_error(p.err, kDevErrEmptyWait);
-            *(volatile int*)abort_flag = 1;
+    if (n_tiles > 0 && lane == 0) {
+      prefetch_tmap(&tm_q);
+      prefetch_tmap(&tm_k);
+      prefetch_tmap(&tm_v);
+      mbar_arrive_expect_tx(q_full, kQBytes);
+      tma_load_3d(sQ, &tm_q, 0, (int)l0, (int)n, q_full);
+      tma_load_3d(sQ + kBM * 128, &tm_q, 64, (int)l0, (int)n, q_full);
+      const int kvh_i = (int)kvh, b_i = (int)b;
+      const int32_t* bt_row = p.dense ? nullptr : p.block_table + b * p.mp;
+      const int mp = (int)p.mp, P = (int)p.P;
+      constexpr int kPagesPerTile = kBN / 16;  // paged path: page_size == 16
+      int ids_k[kPagesPerTile], ids_v[kPagesPerTile];  // page ids of tile t (K) and t-1 (V)
+      int k_issued = 0, v_issued = 0;
+      // issue the copies of one 64-token K or V tile into `dst`, completing on `full`
+      auto issue = [&](const CUtensorMap* tm, uint8_t* dst, uint64_t* full, int j, const int* pid) {
+        mbar_arrive_expect_tx(full, kTileBytes);
+        if (p.dense) {
+          tma_load_4d(dst, tm, 0, j * kBN, kvh_i, b_i, full);
+          tma_load_4d(dst + kBN * 128, tm, 64, j * kBN, kvh_i, b_i, full);
+        } else {
+#pragma unroll
+          for (int g = 0; g < kPagesPerTile; ++g) {
+            tma_load_4d(dst + g * 16 * 128, tm, 0, 0, kvh_i, pid[g], full);
+            tma_load_4d(dst + kBN * 128 + g * 16 * 128, tm, 64, 0, kvh_i, pid[g], full);
           }
-          return false;
         }
-        if (lane == 0) mbar_arrive_expect_tx(full, kTileBytes);
-        __syncwarp();
-        uint8_t* dst = (is_k ? sK : sV) + s * kTileBytes;
-        const CUtensorMap* tm = is_k ? &tm_k : &tm_v;
-        for (int t = lane; t < 2 * boxes; t += 32) {
-          const int half = t / boxes, bx = t % boxes;
-          const int64_t tok0 = (int64_t)j * kBN + (int64_t)bx * p.box_rows;
-          int pid, slot0;
-          if (p.dense) {
-            pid = (int)b;
-            slot0 = (int)tok0;
-          } else {
-            const int64_t pidx = tok0 / p.ps;
-            int64_t id = pidx < p.mp ? (int64_t)p.block_table[b * p.mp + pidx] : -1;
-            if (id < 0 || id >= p.P) id = p.P;  // hole: out-of-range page, TMA fills zeros
-            pid = (int)id;
-            slot0 = (int)(tok0 % p.ps);
-          }
-          const uint32_t off = (uint32_t)(half * kBN * 128 + bx * p.box_rows * 128);
-          tma_load_4d(dst + off, tm, half * 64, slot0, (int)kvh, pid, full);
-        }
-        if (is_k) k_issued = j + 1; else v_issued = j + 1;
-        return true;
       };
       bool ok = true;
-      for (int t = 0; ok && t <= n_tiles; ++t) {
-        if (t < n_tiles) ok = load_tile(true, t);
-        if (ok && t >= 1) ok = load_tile(false, t - 1);
-      }
-      if (lane == 0) {  // drain: every issued load lands before the CTA may exit
-        if (!mbar_wait(q_full, 0)) record_error(p.err, kDevErrDrainWait);
-        auto drain = [&](uint64_t* full, int ns, int issued) {
-          for (int s = 0; s < ns && s < issued; ++s) {
-            const int last = s + ((issued - 1 - s) / ns) * ns;
-            if (!mbar_wait(&full[s], (last / ns) & 1)) record_error(p.err, kDevErrDrainWait);
+      for (int t = 0; t <= n_tiles; ++t) {
+        if (t < n_tiles) {  // K_t
+          const int s = t % kKStages;
+          if (t >= kKStages && !mbar_wait(&k_empty[s], ((t / kKStages) & 1) ^ 1)) {
+            ok = false;
+            break;
           }
-        };
-        drain(k_full, kKStages, k_issued);
-        drain(v_full, kVStages, v_issued);
+          if (!p.dense) {
+#pragma unroll
+            for (int g = 0; g < kPagesPerTile; ++g) {
+              const int pidx = t * kPagesPerTile + g;
+              int id = pidx < mp ? bt_row[pidx] : -1;
+              ids_k[g] = (id < 0 || id >= P) ? P : id;  // hole: out-of-range page, TMA fills zeros
+            }
+          }
+          issue(&tm_k, sK + s * kTileBytes, &k_full[s], t, ids_k);
+          k_issued = t + 1;
+        }
+        if (t >= 1) {  // V_{t-1}
+          const int j = t - 1, s = j % kVStages;
+          if (j >= kVStages && !mbar_wait(&v_empty[s], ((j / kVStages) & 1) ^ 1)) {
+            ok = false;
+            break;
+          }
+          issue(&tm_v, sV + s * kTileBytes, &v_full[s], j, ids_v);
+          v_issued = j + 1;
+        }
+#pragma unroll
+        for (int g = 0; g < kPagesPerTile; ++g) ids_v[g] = ids_k[g];
+        if (*(volatile int*)abort_flag) break;
       }
+      if (!ok) {
+        record_error(p.err, kDevErrEmptyWait);
+        *(volatile int*)abort_flag = 1;
+      }
+      // drain: every issued load lands before the CTA may exit
+      if (!mbar_wait(q_full, 0)) record_error(p.err, kDevErrDrainWait);
+      auto drain = [&](uint64_t* full, int ns, int issued) {
+        for (int s = 0; s < ns && s < issued; ++s) {
+          const int last = s + ((issued - 1 - s) / ns) * ns;
+          if (!mbar_wait(&full[s], (last / ns) & 1)) record_error(p.err, kDevErrDrainWait);
+        }
+      };
+      drain(k_full, kKStages, k_issued);
+      drain(v_full, kVStages, v_issued);
     }
   } else if (warp == 5) {
     // ---------------------------------------------------------------- MMA issuer
     if (n_tiles > 0 && lane == 0) {
       const uint32_t id_qk = idesc<T>(false, kBN);
       const uint32_t id_pv = idesc<T>(true, kD);
-      const uint32_t q_addr = smem_u32(sQ);
+      // Descriptors of the first 16-column slice of Q, K stage 0 and V stage 0; a byte
+      // offset o inside shared memory adds o >> 4 to the start-address field.
+      const uint64_t dq = smem_desc(smem_u32(sQ), 16, 1024);
+      const uint64_t dk = smem_desc(smem_u32(sK), 16, 1024);
+      const uint64_t dv = smem_desc(smem_u32(sV), kBN * 128, 1024);
       bool ok = mbar_wait(q_full, 0);
       auto issue_s = [&](int j) -> bool {
         const int s = j % kKStages;
         if (!mbar_wait(&k_full[s], (j / kKStages) & 1)) return false;
         tc_fence_after();
-        const uint32_t k_addr = smem_u32(sK + s * kTileBytes);
+        const uint64_t dks = dk + (uint64_t)((s * kTileBytes) >> 4);
+        const uint32_t td = tmem + (uint32_t)((j & 1) * kBN);
 #pragma unroll
         for (int ks = 0; ks < kD / 16; ++ks) {
-          const uint64_t da = smem_desc(q_addr + (uint32_t)((ks >> 2) * (kBM * 128) + (ks & 3) * 32), 16, 1024);
-          const uint64_t db = smem_desc(k_addr + (uint32_t)((ks >> 2) * (kBN * 128) + (ks & 3) * 32), 16, 1024);
-          mma_f16(tmem + (uint32_t)((j & 1) * kBN), da, db, id_qk, ks > 0 ? 1u : 0u);
+          // 16-column K slice ks: 64-column half ks/4 (kBM or kBN rows of 128 B), 32 B per slice
+          const uint64_t da = dq + (uint64_t)((((ks >> 2) * (kBM * 128)) + (ks & 3) * 32) >> 4);
+          const uint64_t db = dks + (uint64_t)((((ks >> 2) * (kBN * 128)) + (ks & 3) * 32) >> 4);
+          mma_f16(td, da, db, id_qk, ks > 0 ? 1u : 0u);
         }
         mma_commit(&s_full[j & 1]);
         mma_commit(&k_empty[s]);
@@ -340,12 +372,12 @@ __global__ void __launch_bounds__(kThreads, 2)
           break;
         }
         tc_fence_after();
-        const uint32_t v_addr = smem_u32(sV + s * kTileBytes);
+        const uint64_t dvs = dv + (uint64_t)((s * kTileBytes) >> 4);
         const uint32_t tp = tmem + (uint32_t)((j & 1) * kBN);
 #pragma unroll
         for (int ks = 0; ks < kBN / 16; ++ks) {
           // V is MN-major: 64-column halves kBN*128 bytes apart (LBO), 8-token groups 1024 apart (SBO)
-          const uint64_t db = smem_desc(v_addr + (uint32_t)(ks * 16 * 128), kBN * 128, 1024);
+          const uint64_t db = dvs + (uint64_t)((ks * 16 * 128) >> 4);
           mma_f16_ts(tO, tp + (uint32_t)(ks * 8), db, id_pv, (j > 0 || ks > 0) ? 1u : 0u);
           if (split) mma_f16_ts(tO, tp + (uint32_t)(kBN / 2 + ks * 8), db, id_pv, 1u);
         }
@@ -411,9 +443,16 @@ __global__ void __launch_bounds__(kThreads, 2)
           }
         }
       }
-      float mx = sv[0];
+      // row max as a tree (8 independent chains), not one 64-long dependency chain
+      float mv[8];
 #pragma unroll
-      for (int c = 1; c < kBN; ++c) mx = fmaxf(mx, sv[c]);
+      for (int x = 0; x < 8; ++x) mv[x] = sv[x];
+#pragma unroll
+      for (int c = 8; c < kBN; c += 8) {
+#pragma unroll
+        for (int x = 0; x < 8; ++x) mv[x] = fmaxf(mv[x], sv[c + x]);
+      }
+      const float mx = fmaxf(fmaxf(fmaxf(mv[0], mv[1]), fmaxf(mv[2], mv[3])), fmaxf(fmaxf(mv[4], mv[5]), fmaxf(mv[6], mv[7])));
       const float mx_s = mx * sl2;
       // lazy max: keep the old reference max unless the new one exceeds it by > 8
       float m_ref = m;
@@ -424,19 +463,18 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       const float mu = m_ref == -INFINITY ? 0.f : m_ref;
       const float alpha = ex2_ftz(m - mu);  // 0 when m == -inf
-      float r0 = 0.f, r1 = 0.f, r2 = 0.f, r3 = 0.f;
+      float rv[8];
 #pragma unroll
-      for (int c = 0; c < kBN; c += 4) {
-        sv[c] = ex2_ftz(fmaf(sv[c], sl2, -mu));
-        sv[c + 1] = ex2_ftz(fmaf(sv[c + 1], sl2, -mu));
-        sv[c + 2] = ex2_ftz(fmaf(sv[c + 2], sl2, -mu));
-        sv[c + 3] = ex2_ftz(fmaf(sv[c + 3], sl2, -mu));
-        r0 += sv[c];
-        r1 += sv[c + 1];
-        r2 += sv[c + 2];
-        r3 += sv[c + 3];
+      for (int x = 0; x < 8; ++x) rv[x] = 0.f;
+#pragma unroll
+      for (int c = 0; c < kBN; c += 8) {
+#pragma unroll
+        for (int x = 0; x < 8; ++x) {
+          sv[c + x] = ex2_ftz(fmaf(sv[c + x], sl2, -mu));
+          rv[x] += sv[c + x];
+        }
       }
-      const float rs = (r0 + r1) + (r2 + r3);
+      const float rs = ((rv[0] + rv[1]) + (rv[2] + rv[3])) + ((rv[4] + rv[5]) + (rv[6] + rv[7]));
       lsum = (m == -INFINITY ? 0.f : lsum * alpha) + rs;
       m = m_ref;
       if (__any_sync(0xffffffffu, rescale)) {
@@ -461,14 +499,15 @@ __global__ void __launch_bounds__(kThreads, 2)
       {
         uint32_t hi[32];
 #pragma unroll
-        for (int x = 0; x < 32; ++x) hi[x] = pack2<T>(sv[2 * x], sv[2 * x + 1]);
+        for (int x = 0; x < 32; ++x) hi[x] = cvt_pack<T>(sv[2 * x], sv[2 * x + 1]);
         tmem_st32u(tS, hi);
         if (split) {
           uint32_t lo[32];
 #pragma unroll
           for (int x = 0; x < 32; ++x) {
-            const __nv_bfloat162 hh = *reinterpret_cast<const __nv_bfloat162*>(&hi[x]);
-            lo[x] = pack2<T>(sv[2 * x] - __low2float(hh), sv[2 * x + 1] - __high2float(hh));
+            // bf16 -> f32 is exact: the bf16 bits become the high half of the f32
+            const float h0 = __uint_as_float(hi[x] << 16), h1 = __uint_as_float(hi[x] & 0xFFFF0000u);
+            lo[x] = cvt_pack<T>(sv[2 * x] - h0, sv[2 * x + 1] - h1);
           }
           tmem_st32u(tS + kBN / 2, lo);
         }

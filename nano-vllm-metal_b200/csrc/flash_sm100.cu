@@ -129,6 +129,17 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
   return __all_sync(0xffffffffu, ok) != 0;
 }
 
+// One lane of the (converged) warp: PTX elect.sync.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
 // 2^x on the MUFU unit (PTX ex2.approx.ftz.f32): -inf gives +0, subnormal results flush to 0.
 __device__ __forceinline__ float ex2_ftz(float x) {
   float y;
@@ -257,16 +268,19 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   if (warp == 4) {
     // ---------------------------------------------------------------- producer
-    // One thread, straight-line: this warp shares its scheduler with two softmax warps
-    // that issue nearly every cycle, so each instruction here costs several cycles.
-    // Loads run in the order the MMA warp consumes them: K_0, K_1, V_0, K_2, V_1, ...
-    if (n_tiles > 0 && lane == 0) {
-      prefetch_tmap(&tm_q);
-      prefetch_tmap(&tm_k);
-      prefetch_tmap(&tm_v);
-      mbar_arrive_expect_tx(q_full, kQBytes);
-      tma_load_3d(sQ, &tm_q, 0, (int)l0, (int)n, q_full);
-      tma_load_3d(sQ + kBM * 128, &tm_q, 64, (int)l0, (int)n, q_full);
+    // The whole warp runs the loop (warp-uniform values stay on the uniform datapath)
+    // and one elected lane issues the copies.  Loads run in the order the MMA warp
+    // consumes them: K_0, K_1, V_0, K_2, V_1, ...
+    if (n_tiles > 0) {
+      const bool leader = elect_one();
+      if (leader) {
+        prefetch_tmap(&tm_q);
+        prefetch_tmap(&tm_k);
+        prefetch_tmap(&tm_v);
+        mbar_arrive_expect_tx(q_full, kQBytes);
+        tma_load_3d(sQ, &tm_q, 0, (int)l0, (int)n, q_full);
+        tma_load_3d(sQ + kBM * 128, &tm_q, 64, (int)l0, (int)n, q_full);
+      }
       const int kvh_i = (int)kvh, b_i = (int)b;
       const int32_t* bt_row = p.dense ? nullptr : p.block_table + b * p.mp;
       const int mp = (int)p.mp, P = (int)p.P;
@@ -275,23 +289,26 @@ __global__ void __launch_bounds__(kThreads, 2)
       int k_issued = 0, v_issued = 0;
       // issue the copies of one 64-token K or V tile into `dst`, completing on `full`
       auto issue = [&](const CUtensorMap* tm, uint8_t* dst, uint64_t* full, int j, const int* pid) {
-        mbar_arrive_expect_tx(full, kTileBytes);
-        if (p.dense) {
-          tma_load_4d(dst, tm, 0, j * kBN, kvh_i, b_i, full);
-          tma_load_4d(dst + kBN * 128, tm, 64, j * kBN, kvh_i, b_i, full);
-        } else {
+        if (leader) {
+          mbar_arrive_expect_tx(full, kTileBytes);
+          if (p.dense) {
+            tma_load_4d(dst, tm, 0, j * kBN, kvh_i, b_i, full);
+            tma_load_4d(dst + kBN * 128, tm, 64, j * kBN, kvh_i, b_i, full);
+          } else {
 #pragma unroll
-          for (int g = 0; g < kPagesPerTile; ++g) {
-            tma_load_4d(dst + g * 16 * 128, tm, 0, 0, kvh_i, pid[g], full);
-            tma_load_4d(dst + kBN * 128 + g * 16 * 128, tm, 64, 0, kvh_i, pid[g], full);
+            for (int g = 0; g < kPagesPerTile; ++g) {
+              tma_load_4d(dst + g * 16 * 128, tm, 0, 0, kvh_i, pid[g], full);
+              tma_load_4d(dst + kBN * 128 + g * 16 * 128, tm, 64, 0, kvh_i, pid[g], full);
+            }
           }
         }
+        __syncwarp();
       };
       bool ok = true;
       for (int t = 0; t <= n_tiles; ++t) {
         if (t < n_tiles) {  // K_t
           const int s = t % kKStages;
-          if (t >= kKStages && !mbar_wait(&k_empty[s], ((t / kKStages) & 1) ^ 1)) {
+          if (t >= kKStages && !warp_wait(&k_empty[s], ((t / kKStages) & 1) ^ 1)) {
             ok = false;
             break;
           }
@@ -308,7 +325,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         if (t >= 1) {  // V_{t-1}
           const int j = t - 1, s = j % kVStages;
-          if (j >= kVStages && !mbar_wait(&v_empty[s], ((j / kVStages) & 1) ^ 1)) {
+          if (j >= kVStages && !warp_wait(&v_empty[s], ((j / kVStages) & 1) ^ 1)) {
             ok = false;
             break;
           }
@@ -317,26 +334,32 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
 #pragma unroll
         for (int g = 0; g < kPagesPerTile; ++g) ids_v[g] = ids_k[g];
-        if (*(volatile int*)abort_flag) break;
+        if (__any_sync(0xffffffffu, *(volatile int*)abort_flag != 0)) break;
       }
-      if (!ok) {
-        record_error(p.err, kDevErrEmptyWait);
-        *(volatile int*)abort_flag = 1;
-      }
-      // drain: every issued load lands before the CTA may exit
-      if (!mbar_wait(q_full, 0)) record_error(p.err, kDevErrDrainWait);
-      auto drain = [&](uint64_t* full, int ns, int issued) {
-        for (int s = 0; s < ns && s < issued; ++s) {
-          const int last = s + ((issued - 1 - s) / ns) * ns;
-          if (!mbar_wait(&full[s], (last / ns) & 1)) record_error(p.err, kDevErrDrainWait);
+      if (leader) {
+        if (!ok) {
+          record_error(p.err, kDevErrEmptyWait);
+          *(volatile int*)abort_flag = 1;
         }
-      };
-      drain(k_full, kKStages, k_issued);
-      drain(v_full, kVStages, v_issued);
+        // drain: every issued load lands before the CTA may exit
+        if (!mbar_wait(q_full, 0)) record_error(p.err, kDevErrDrainWait);
+        auto drain = [&](uint64_t* full, int ns, int issued) {
+          for (int s = 0; s < ns && s < issued; ++s) {
+            const int last = s + ((issued - 1 - s) / ns) * ns;
+            if (!mbar_wait(&full[s], (last / ns) & 1)) record_error(p.err, kDevErrDrainWait);
+          }
+        };
+        drain(k_full, kKStages, k_issued);
+        drain(v_full, kVStages, v_issued);
+      }
+      __syncwarp();
     }
   } else if (warp == 5) {
     // ---------------------------------------------------------------- MMA issuer
-    if (n_tiles > 0 && lane == 0) {
+    // The whole warp waits and loops; one elected lane issues the MMAs and the commits
+    // (a commit tracks the MMAs of the thread that issues it, so it is always the same lane).
+    if (n_tiles > 0) {
+      const bool leader = elect_one();
       const uint32_t id_qk = idesc<T>(false, kBN);
       const uint32_t id_pv = idesc<T>(true, kD);
       // Descriptors of the first 16-column slice of Q, K stage 0 and V stage 0; a byte
@@ -344,22 +367,25 @@ __global__ void __launch_bounds__(kThreads, 2)
       const uint64_t dq = smem_desc(smem_u32(sQ), 16, 1024);
       const uint64_t dk = smem_desc(smem_u32(sK), 16, 1024);
       const uint64_t dv = smem_desc(smem_u32(sV), kBN * 128, 1024);
-      bool ok = mbar_wait(q_full, 0);
+      bool ok = warp_wait(q_full, 0);
       auto issue_s = [&](int j) -> bool {
         const int s = j % kKStages;
-        if (!mbar_wait(&k_full[s], (j / kKStages) & 1)) return false;
+        if (!warp_wait(&k_full[s], (j / kKStages) & 1)) return false;
         tc_fence_after();
         const uint64_t dks = dk + (uint64_t)((s * kTileBytes) >> 4);
         const uint32_t td = tmem + (uint32_t)((j & 1) * kBN);
+        if (leader) {
 #pragma unroll
-        for (int ks = 0; ks < kD / 16; ++ks) {
-          // 16-column K slice ks: 64-column half ks/4 (kBM or kBN rows of 128 B), 32 B per slice
-          const uint64_t da = dq + (uint64_t)((((ks >> 2) * (kBM * 128)) + (ks & 3) * 32) >> 4);
-          const uint64_t db = dks + (uint64_t)((((ks >> 2) * (kBN * 128)) + (ks & 3) * 32) >> 4);
-          mma_f16(td, da, db, id_qk, ks > 0 ? 1u : 0u);
+          for (int ks = 0; ks < kD / 16; ++ks) {
+            // 16-column K slice ks: 64-column half ks/4 (kBM or kBN rows of 128 B), 32 B per slice
+            const uint64_t da = dq + (uint64_t)((((ks >> 2) * (kBM * 128)) + (ks & 3) * 32) >> 4);
+            const uint64_t db = dks + (uint64_t)((((ks >> 2) * (kBN * 128)) + (ks & 3) * 32) >> 4);
+            mma_f16(td, da, db, id_qk, ks > 0 ? 1u : 0u);
+          }
+          mma_commit(&s_full[j & 1]);
+          mma_commit(&k_empty[s]);
         }
-        mma_commit(&s_full[j & 1]);
-        mma_commit(&k_empty[s]);
+        __syncwarp();
         return true;
       };
       if (ok) ok = issue_s(0);
@@ -367,26 +393,29 @@ __global__ void __launch_bounds__(kThreads, 2)
       for (int j = 0; ok && j < n_tiles; ++j) {
         // P_j (over S_j's TMEM columns) written by the softmax warps, V_j landed
         const int s = j % kVStages;
-        if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1) || !mbar_wait(&v_full[s], (j / kVStages) & 1)) {
+        if (!warp_wait(&p_full[j & 1], (j >> 1) & 1) || !warp_wait(&v_full[s], (j / kVStages) & 1)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint64_t dvs = dv + (uint64_t)((s * kTileBytes) >> 4);
         const uint32_t tp = tmem + (uint32_t)((j & 1) * kBN);
+        if (leader) {
 #pragma unroll
-        for (int ks = 0; ks < kBN / 16; ++ks) {
-          // V is MN-major: 64-column halves kBN*128 bytes apart (LBO), 8-token groups 1024 apart (SBO)
-          const uint64_t db = dvs + (uint64_t)((ks * 16 * 128) >> 4);
-          mma_f16_ts(tO, tp + (uint32_t)(ks * 8), db, id_pv, (j > 0 || ks > 0) ? 1u : 0u);
-          if (split) mma_f16_ts(tO, tp + (uint32_t)(kBN / 2 + ks * 8), db, id_pv, 1u);
+          for (int ks = 0; ks < kBN / 16; ++ks) {
+            // V is MN-major: 64-column halves kBN*128 bytes apart (LBO), 8-token groups 1024 apart (SBO)
+            const uint64_t db = dvs + (uint64_t)((ks * 16 * 128) >> 4);
+            mma_f16_ts(tO, tp + (uint32_t)(ks * 8), db, id_pv, (j > 0 || ks > 0) ? 1u : 0u);
+            if (split) mma_f16_ts(tO, tp + (uint32_t)(kBN / 2 + ks * 8), db, id_pv, 1u);
+          }
+          mma_commit(o_done);
+          mma_commit(&v_empty[s]);
         }
-        mma_commit(o_done);
-        mma_commit(&v_empty[s]);
+        __syncwarp();
         // S_{j+2} reuses S_j's TMEM columns, which hold P_j: wait until PV_j has
         // finished reading them (o_done phase j) before overwriting.
         if (j + 2 < n_tiles) {
-          if (!mbar_wait(o_done, j & 1)) {
+          if (!warp_wait(o_done, j & 1)) {
             ok = false;
             break;
           }
@@ -394,11 +423,14 @@ __global__ void __launch_bounds__(kThreads, 2)
           ok = issue_s(j + 2);
         }
       }
-      if (!ok) {
-        record_error(p.err, kDevErrMmaWait);
-        *(volatile int*)abort_flag = 1;
+      if (leader) {
+        if (!ok) {
+          record_error(p.err, kDevErrMmaWait);
+          *(volatile int*)abort_flag = 1;
+        }
+        mma_commit(mma_done);
       }
-      mma_commit(mma_done);
+      __syncwarp();
     }
   } else {
     // ---------------------------------------------------------------- softmax warps 0-3

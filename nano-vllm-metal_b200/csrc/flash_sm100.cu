@@ -147,6 +147,39 @@ __device__ __forceinline__ float ex2_ftz(float x) {
   return y;
 }
 
+// Pairs q (keys 2q, 2q+1 of a 64-key tile) whose exponentials run on the FMA pipe.
+constexpr uint32_t kEmuPairs = 0x88888888u;  // every fourth pair: 25%
+
+// 2^x for two floats on the FMA pipe: n = round(x) through the 1.5 * 2^23 rounding
+// constant, f = x - n in [-0.5, 0.5] (exact), 2^f from a polynomial, then n is added to
+// the exponent field.  The coefficients are a near-minimax fit of 2^f on [-0.5, 0.5]
+// for relative error (iteratively reweighted least squares): degree 3 (7.5e-5, far below
+// the bf16 rounding of P that follows) for bf16, degree 4 (2.7e-6) for fp16.  Inputs
+// below -125 (masked scores, -inf) give 2^-125.
+template <typename T>
+__device__ __forceinline__ float2 exp2_fma2(float2 x) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  x.x = fmaxf(x.x, -125.f);
+  x.y = fmaxf(x.y, -125.f);
+  const float2 t = __fadd2_rn(x, make_float2(kRound, kRound));
+  const float2 n = __fadd2_rn(t, make_float2(-kRound, -kRound));
+  const float2 f = __ffma2_rn(n, make_float2(-1.f, -1.f), x);
+  float2 p;
+  if (std::is_same<T, __half>::value) {
+    p = __ffma2_rn(make_float2(0.009570102f, 0.009570102f), f, make_float2(0.05591786f, 0.05591786f));
+    p = __ffma2_rn(p, f, make_float2(0.24024744f, 0.24024744f));
+    p = __ffma2_rn(p, f, make_float2(0.69312179f, 0.69312179f));
+    p = __ffma2_rn(p, f, make_float2(0.99999928f, 0.99999928f));
+  } else {
+    p = __ffma2_rn(make_float2(0.05517167f, 0.05517167f), f, make_float2(0.24261113f, 0.24261113f));
+    p = __ffma2_rn(p, f, make_float2(0.69326097f, 0.69326097f));
+    p = __ffma2_rn(p, f, make_float2(0.99992806f, 0.99992806f));
+  }
+  // t's low mantissa bits hold n (two's complement); << 23 moves them to the exponent
+  return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(t.x) << 23)),
+                     __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23)));
+}
+
 // Round two floats to a packed 16-bit pair in one instruction: a in the low half, b in the high.
 template <typename T>
 __device__ __forceinline__ uint32_t cvt_pack(float a, float b);
@@ -495,18 +528,37 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       const float mu = m_ref == -INFINITY ? 0.f : m_ref;
       const float alpha = ex2_ftz(m - mu);  // 0 when m == -inf
-      float rv[8];
+      // p = 2^(s * sl2 - mu) on packed pairs.  Most exponentials run on the MUFU unit;
+      // outside split tiles the pairs selected by kEmuPairs run on the FMA pipe instead
+      // (exp2_fma2), which keeps MUFU from setting the tile rate.
+      const float2 sl2v = make_float2(sl2, sl2), nmu = make_float2(-mu, -mu);
+      float2 acc[4];
 #pragma unroll
-      for (int x = 0; x < 8; ++x) rv[x] = 0.f;
+      for (int x = 0; x < 4; ++x) acc[x] = make_float2(0.f, 0.f);
+      if (split) {
 #pragma unroll
-      for (int c = 0; c < kBN; c += 8) {
+        for (int q = 0; q < kBN / 2; ++q) {
+          const float2 x2 = __ffma2_rn(make_float2(sv[2 * q], sv[2 * q + 1]), sl2v, nmu);
+          const float2 e = make_float2(ex2_ftz(x2.x), ex2_ftz(x2.y));
+          sv[2 * q] = e.x;
+          sv[2 * q + 1] = e.y;
+          acc[q & 3] = __fadd2_rn(acc[q & 3], e);
+        }
+      } else {
 #pragma unroll
-        for (int x = 0; x < 8; ++x) {
-          sv[c + x] = ex2_ftz(fmaf(sv[c + x], sl2, -mu));
-          rv[x] += sv[c + x];
+        for (int q = 0; q < kBN / 2; ++q) {
+          const float2 x2 = __ffma2_rn(make_float2(sv[2 * q], sv[2 * q + 1]), sl2v, nmu);
+          const float2 e = ((kEmuPairs >> q) & 1u) ? exp2_fma2<T>(x2) : make_float2(ex2_ftz(x2.x), ex2_ftz(x2.y));
+          sv[2 * q] = e.x;
+          sv[2 * q + 1] = e.y;
+          acc[q & 3] = __fadd2_rn(acc[q & 3], e);
         }
       }
-      const float rs = ((rv[0] + rv[1]) + (rv[2] + rv[3])) + ((rv[4] + rv[5]) + (rv[6] + rv[7]));
+      const float2 a01 = __fadd2_rn(__fadd2_rn(acc[0], acc[1]), __fadd2_rn(acc[2], acc[3]));
+      // A row with no visible key yet keeps a zero sum (so it ends as zeros): exp2_fma2
+      // turns its -inf scores into 2^-125, not 0.  Next to a visible key's p >= 2^-8,
+      // 2^-125 is nothing.
+      const float rs = m_ref == -INFINITY ? 0.f : a01.x + a01.y;
       lsum = (m == -INFINITY ? 0.f : lsum * alpha) + rs;
       m = m_ref;
       if (__any_sync(0xffffffffu, rescale)) {

@@ -60,3 +60,47 @@ def test_repeated_calls_stable(cuda):
     for _ in range(5):
         assert torch.equal(flash_attention(q, k, v, mask="causal"), first)
     assert nv.device_error(cuda) == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_paged_rows_without_keys(cuda, oracle, dtype):
+    """Rows that see no key come out as zeros: context shorter than the chunk (causal
+    limit below 0), an empty sequence, and rows whose visible keys are all holes."""
+    gen = torch.Generator().manual_seed(77)
+    B, Hq, Hkv, L, D, ps = 3, 8, 2, 192, 128, 16
+    ctx = torch.tensor([100, 0, 300], dtype=torch.int32)
+    pages = [(int(c) + ps - 1) // ps for c in ctx]
+    MP = max(pages)
+    P = sum(pages) + 2
+    perm = torch.randperm(P, generator=gen)
+    bt = torch.full((B, MP), -1, dtype=torch.int32)
+    k = 0
+    for b in range(B):
+        bt[b, :pages[b]] = perm[k:k + pages[b]].to(torch.int32)
+        k += pages[b]
+    bt[2, :8] = -1  # keys 0..127 of sequence 2 missing: its rows 0..19 see only holes
+    kp = torch.randn(P, Hkv, ps, D, generator=gen).to(dtype)
+    vp = torch.randn(P, Hkv, ps, D, generator=gen).to(dtype)
+    q = torch.randn(B, Hq, L, D, generator=gen).to(dtype)
+    prob = dict(q=q.cuda(), kp=kp.cuda(), vp=vp.cuda(), ks=None, vs=None, bt=bt.cuda(), cl=ctx.cuda(), ps=ps)
+    out = paged_attention(prob["q"], prob["kp"], prob["vp"], prob["bt"], prob["cl"], ps, mask="causal")
+    ref = oracle_paged(oracle, prob)
+    assert_close(out, ref, TOL16)
+    got = out.cpu()
+    assert torch.count_nonzero(got[0, :, :92]) == 0
+    assert torch.count_nonzero(got[1]) == 0
+    assert torch.count_nonzero(got[2, :, :20]) == 0
+    assert nv.device_error(cuda) == 0
+
+
+def test_dense_negative_scale(cuda, oracle):
+    """A scale <= 0 is outside the tcgen05 kernel's contract (it takes row maxima
+    before scaling); such calls take another kernel and still match."""
+    gen = torch.Generator().manual_seed(3)
+    q = torch.randn(1, 4, 256, 128, generator=gen).bfloat16()
+    k = torch.randn(1, 2, 256, 128, generator=gen).bfloat16()
+    v = torch.randn(1, 2, 256, 128, generator=gen).bfloat16()
+    out = flash_attention(q.cuda(), k.cuda(), v.cuda(), scale=-0.05, mask="causal", out_dtype=torch.float32)
+    ref = oracle.flash_attention_ref(q.float().numpy(), k.float().numpy(), v.float().numpy(), scale=-0.05,
+                                     mask="causal", nthreads=8)
+    assert_close(out, ref, TOL16)

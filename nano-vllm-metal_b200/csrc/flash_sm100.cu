@@ -129,6 +129,18 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
   return __all_sync(0xffffffffu, ok) != 0;
 }
 
+// TMA tensor store of one box from shared memory (bulk-group completion).
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(src))
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until every committed bulk store has finished reading shared memory.
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 // One lane of the (converged) warp: PTX elect.sync.
 __device__ __forceinline__ bool elect_one() {
   uint32_t pred = 0;
@@ -224,7 +236,8 @@ __device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t (&r)[3
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 2)
     flash_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                       const __grid_constant__ CUtensorMap tm_v, const Sm100Params p) {
+                       const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
+                       const Sm100Params p) {
   constexpr bool kSplit = std::is_same<T, __nv_bfloat16>::value;  // bf16 P = hi + lo
   extern __shared__ __align__(1024) uint8_t smem[];
   if ((smem_u32(smem) & 1023u) != 0) {  // 128B-swizzled tiles need a 1024-byte aligned base
@@ -266,24 +279,94 @@ __global__ void __launch_bounds__(kThreads, 2)
   if (ctx <= 0 || need < 0) need = 0;
   const int n_tiles = (int)((need + kBN - 1) / kBN);
 
-  if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
-    for (int s = 0; s < kKStages; ++s) {
-      mbar_init(&k_full[s], 1);
-      mbar_init(&k_empty[s], 1);
+  // ---------------------------------------------------------------- producer (warp 4)
+  // The whole warp runs the loop (warp-uniform values stay on the uniform datapath) and
+  // one elected lane issues the copies.  Loads run in the order the MMA warp consumes
+  // them: K_0, K_1, V_0, K_2, V_1, ...  The first kKStages iterations need no free stage:
+  // the producer initialises the mbarriers itself and issues them before the block
+  // barrier, so TMEM allocation and the other warps' set-up overlap the first copies.
+  bool prod_leader = false;
+  const int kvh_i = (int)kvh, b_i = (int)b;
+  const int32_t* bt_row = p.dense ? nullptr : p.block_table + b * p.mp;
+  constexpr int kPagesPerTile = kBN / 16;  // paged path: page_size == 16
+  int ids_k[kPagesPerTile], ids_v[kPagesPerTile];  // page ids of tile t (K) and t-1 (V)
+  int k_issued = 0, v_issued = 0, t_next = 0;
+  // issue the copies of one 64-token K or V tile into `dst`, completing on `full`
+  auto issue = [&](const CUtensorMap* tm, uint8_t* dst, uint64_t* full, int j, const int* pid) {
+    if (prod_leader) {
+      mbar_arrive_expect_tx(full, kTileBytes);
+      if (p.dense) {
+        tma_load_4d(dst, tm, 0, j * kBN, kvh_i, b_i, full);
+        tma_load_4d(dst + kBN * 128, tm, 64, j * kBN, kvh_i, b_i, full);
+      } else {
+#pragma unroll
+        for (int g = 0; g < kPagesPerTile; ++g) {
+          tma_load_4d(dst + g * 16 * 128, tm, 0, 0, kvh_i, pid[g], full);
+          tma_load_4d(dst + kBN * 128 + g * 16 * 128, tm, 64, 0, kvh_i, pid[g], full);
+        }
+      }
     }
-    for (int s = 0; s < kVStages; ++s) {
-      mbar_init(&v_full[s], 1);
-      mbar_init(&v_empty[s], 1);
+    __syncwarp();
+  };
+  // loop iteration t: K_t (t < n_tiles) and V_{t-1} (t >= 1); false if a wait expired
+  auto produce = [&](int t) -> bool {
+    if (t < n_tiles) {
+      const int s = t % kKStages;
+      if (t >= kKStages && !warp_wait(&k_empty[s], ((t / kKStages) & 1) ^ 1)) return false;
+      if (!p.dense) {
+#pragma unroll
+        for (int g = 0; g < kPagesPerTile; ++g) {
+          const int pidx = t * kPagesPerTile + g;
+          int id = pidx < (int)p.mp ? bt_row[pidx] : -1;
+          ids_k[g] = (id < 0 || id >= (int)p.P) ? (int)p.P : id;  // hole: out-of-range page, TMA fills zeros
+        }
+      }
+      issue(&tm_k, sK + s * kTileBytes, &k_full[s], t, ids_k);
+      k_issued = t + 1;
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 128);
+    if (t >= 1) {
+      const int j = t - 1, s = j % kVStages;
+      if (j >= kVStages && !warp_wait(&v_empty[s], ((j / kVStages) & 1) ^ 1)) return false;
+      issue(&tm_v, sV + s * kTileBytes, &v_full[s], j, ids_v);
+      v_issued = j + 1;
     }
-    mbar_init(o_done, 1);
-    mbar_init(mma_done, 1);
-    *abort_flag = 0;
-    fence_mbar_init();
+#pragma unroll
+    for (int g = 0; g < kPagesPerTile; ++g) ids_v[g] = ids_k[g];
+    return true;
+  };
+  static_assert(kVStages + 1 >= kKStages, "iterations t < kKStages must not wait for a V stage");
+
+  if (warp == 4) {
+    prod_leader = elect_one();
+    if (prod_leader) {
+      mbar_init(q_full, 1);
+      for (int s = 0; s < kKStages; ++s) {
+        mbar_init(&k_full[s], 1);
+        mbar_init(&k_empty[s], 1);
+      }
+      for (int s = 0; s < kVStages; ++s) {
+        mbar_init(&v_full[s], 1);
+        mbar_init(&v_empty[s], 1);
+      }
+      for (int i = 0; i < 2; ++i) {
+        mbar_init(&s_full[i], 1);
+        mbar_init(&p_full[i], 128);
+      }
+      mbar_init(o_done, 1);
+      mbar_init(mma_done, 1);
+      *abort_flag = 0;
+      fence_mbar_init();
+      if (n_tiles > 0) {
+        prefetch_tmap(&tm_q);
+        prefetch_tmap(&tm_k);
+        prefetch_tmap(&tm_v);
+        mbar_arrive_expect_tx(q_full, kQBytes);
+        tma_load_3d(sQ, &tm_q, 0, (int)l0, (int)n, q_full);
+        tma_load_3d(sQ + kBM * 128, &tm_q, 64, (int)l0, (int)n, q_full);
+      }
+    }
+    __syncwarp();
+    for (; t_next < kKStages && t_next <= n_tiles && n_tiles > 0; ++t_next) produce(t_next);  // no waits
   }
   if (warp == 5) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
@@ -300,76 +383,16 @@ __global__ void __launch_bounds__(kThreads, 2)
   const bool split = kSplit && min_keys < p.split_below;
 
   if (warp == 4) {
-    // ---------------------------------------------------------------- producer
-    // The whole warp runs the loop (warp-uniform values stay on the uniform datapath)
-    // and one elected lane issues the copies.  Loads run in the order the MMA warp
-    // consumes them: K_0, K_1, V_0, K_2, V_1, ...
     if (n_tiles > 0) {
-      const bool leader = elect_one();
-      if (leader) {
-        prefetch_tmap(&tm_q);
-        prefetch_tmap(&tm_k);
-        prefetch_tmap(&tm_v);
-        mbar_arrive_expect_tx(q_full, kQBytes);
-        tma_load_3d(sQ, &tm_q, 0, (int)l0, (int)n, q_full);
-        tma_load_3d(sQ + kBM * 128, &tm_q, 64, (int)l0, (int)n, q_full);
-      }
-      const int kvh_i = (int)kvh, b_i = (int)b;
-      const int32_t* bt_row = p.dense ? nullptr : p.block_table + b * p.mp;
-      const int mp = (int)p.mp, P = (int)p.P;
-      constexpr int kPagesPerTile = kBN / 16;  // paged path: page_size == 16
-      int ids_k[kPagesPerTile], ids_v[kPagesPerTile];  // page ids of tile t (K) and t-1 (V)
-      int k_issued = 0, v_issued = 0;
-      // issue the copies of one 64-token K or V tile into `dst`, completing on `full`
-      auto issue = [&](const CUtensorMap* tm, uint8_t* dst, uint64_t* full, int j, const int* pid) {
-        if (leader) {
-          mbar_arrive_expect_tx(full, kTileBytes);
-          if (p.dense) {
-            tma_load_4d(dst, tm, 0, j * kBN, kvh_i, b_i, full);
-            tma_load_4d(dst + kBN * 128, tm, 64, j * kBN, kvh_i, b_i, full);
-          } else {
-#pragma unroll
-            for (int g = 0; g < kPagesPerTile; ++g) {
-              tma_load_4d(dst + g * 16 * 128, tm, 0, 0, kvh_i, pid[g], full);
-              tma_load_4d(dst + kBN * 128 + g * 16 * 128, tm, 64, 0, kvh_i, pid[g], full);
-            }
-          }
-        }
-        __syncwarp();
-      };
       bool ok = true;
-      for (int t = 0; t <= n_tiles; ++t) {
-        if (t < n_tiles) {  // K_t
-          const int s = t % kKStages;
-          if (t >= kKStages && !warp_wait(&k_empty[s], ((t / kKStages) & 1) ^ 1)) {
-            ok = false;
-            break;
-          }
-          if (!p.dense) {
-#pragma unroll
-            for (int g = 0; g < kPagesPerTile; ++g) {
-              const int pidx = t * kPagesPerTile + g;
-              int id = pidx < mp ? bt_row[pidx] : -1;
-              ids_k[g] = (id < 0 || id >= P) ? P : id;  // hole: out-of-range page, TMA fills zeros
-            }
-          }
-          issue(&tm_k, sK + s * kTileBytes, &k_full[s], t, ids_k);
-          k_issued = t + 1;
+      for (; t_next <= n_tiles; ++t_next) {
+        if (!produce(t_next)) {
+          ok = false;
+          break;
         }
-        if (t >= 1) {  // V_{t-1}
-          const int j = t - 1, s = j % kVStages;
-          if (j >= kVStages && !warp_wait(&v_empty[s], ((j / kVStages) & 1) ^ 1)) {
-            ok = false;
-            break;
-          }
-          issue(&tm_v, sV + s * kTileBytes, &v_full[s], j, ids_v);
-          v_issued = j + 1;
-        }
-#pragma unroll
-        for (int g = 0; g < kPagesPerTile; ++g) ids_v[g] = ids_k[g];
         if (__any_sync(0xffffffffu, *(volatile int*)abort_flag != 0)) break;
       }
-      if (leader) {
+      if (prod_leader) {
         if (!ok) {
           record_error(p.err, kDevErrEmptyWait);
           *(volatile int*)abort_flag = 1;
@@ -397,32 +420,40 @@ __global__ void __launch_bounds__(kThreads, 2)
       const uint32_t id_pv = idesc<T>(true, kD);
       // Descriptors of the first 16-column slice of Q, K stage 0 and V stage 0; a byte
       // offset o inside shared memory adds o >> 4 to the start-address field.
-      const uint64_t dq = smem_desc(smem_u32(sQ), 16, 1024);
+      // One thread can issue a tcgen05.mma only every ~47 cycles, and descriptor
+      // arithmetic between two MMAs adds ~26 more: the Q descriptors are computed once,
+      // a tile's K or V descriptors in one batch before its MMAs.
+      uint64_t dq[8];
+      {
+        const uint64_t q0 = smem_desc(smem_u32(sQ), 16, 1024);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) dq[ks] = q0 + (uint64_t)((((ks >> 2) * (kBM * 128)) + (ks & 3) * 32) >> 4);
+      }
       const uint64_t dk = smem_desc(smem_u32(sK), 16, 1024);
       const uint64_t dv = smem_desc(smem_u32(sV), kBN * 128, 1024);
       bool ok = warp_wait(q_full, 0);
+      // K_j landed (checked before the wait on PV_{j-2}, which it does not depend on)
+      auto wait_k = [&](int j) -> bool { return warp_wait(&k_full[j % kKStages], (j / kKStages) & 1); };
       auto issue_s = [&](int j) -> bool {
         const int s = j % kKStages;
-        if (!warp_wait(&k_full[s], (j / kKStages) & 1)) return false;
         tc_fence_after();
+        // 16-column K slice ks: 64-column half ks/4 (kBN rows of 128 B), 32 B per slice
         const uint64_t dks = dk + (uint64_t)((s * kTileBytes) >> 4);
+        uint64_t db[8];
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) db[ks] = dks + (uint64_t)((((ks >> 2) * (kBN * 128)) + (ks & 3) * 32) >> 4);
         const uint32_t td = tmem + (uint32_t)((j & 1) * kBN);
         if (leader) {
 #pragma unroll
-          for (int ks = 0; ks < kD / 16; ++ks) {
-            // 16-column K slice ks: 64-column half ks/4 (kBM or kBN rows of 128 B), 32 B per slice
-            const uint64_t da = dq + (uint64_t)((((ks >> 2) * (kBM * 128)) + (ks & 3) * 32) >> 4);
-            const uint64_t db = dks + (uint64_t)((((ks >> 2) * (kBN * 128)) + (ks & 3) * 32) >> 4);
-            mma_f16(td, da, db, id_qk, ks > 0 ? 1u : 0u);
-          }
+          for (int ks = 0; ks < kD / 16; ++ks) mma_f16(td, dq[ks], db[ks], id_qk, ks > 0 ? 1u : 0u);
           mma_commit(&s_full[j & 1]);
           mma_commit(&k_empty[s]);
         }
         __syncwarp();
         return true;
       };
-      if (ok) ok = issue_s(0);
-      if (ok && n_tiles > 1) ok = issue_s(1);
+      if (ok) ok = wait_k(0) && issue_s(0);
+      if (ok && n_tiles > 1) ok = wait_k(1) && issue_s(1);
       for (int j = 0; ok && j < n_tiles; ++j) {
         // P_j (over S_j's TMEM columns) written by the softmax warps, V_j landed
         const int s = j % kVStages;
@@ -431,15 +462,17 @@ __global__ void __launch_bounds__(kThreads, 2)
           break;
         }
         tc_fence_after();
+        // V is MN-major: 64-column halves kBN*128 bytes apart (LBO), 8-token groups 1024 apart (SBO)
         const uint64_t dvs = dv + (uint64_t)((s * kTileBytes) >> 4);
+        uint64_t db[4];
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks) db[ks] = dvs + (uint64_t)((ks * 16 * 128) >> 4);
         const uint32_t tp = tmem + (uint32_t)((j & 1) * kBN);
         if (leader) {
 #pragma unroll
           for (int ks = 0; ks < kBN / 16; ++ks) {
-            // V is MN-major: 64-column halves kBN*128 bytes apart (LBO), 8-token groups 1024 apart (SBO)
-            const uint64_t db = dvs + (uint64_t)((ks * 16 * 128) >> 4);
-            mma_f16_ts(tO, tp + (uint32_t)(ks * 8), db, id_pv, (j > 0 || ks > 0) ? 1u : 0u);
-            if (split) mma_f16_ts(tO, tp + (uint32_t)(kBN / 2 + ks * 8), db, id_pv, 1u);
+            mma_f16_ts(tO, tp + (uint32_t)(ks * 8), db[ks], id_pv, (j > 0 || ks > 0) ? 1u : 0u);
+            if (split) mma_f16_ts(tO, tp + (uint32_t)(kBN / 2 + ks * 8), db[ks], id_pv, 1u);
           }
           mma_commit(o_done);
           mma_commit(&v_empty[s]);
@@ -448,11 +481,10 @@ __global__ void __launch_bounds__(kThreads, 2)
         // S_{j+2} reuses S_j's TMEM columns, which hold P_j: wait until PV_j has
         // finished reading them (o_done phase j) before overwriting.
         if (j + 2 < n_tiles) {
-          if (!warp_wait(o_done, j & 1)) {
+          if (!wait_k(j + 2) || !warp_wait(o_done, j & 1)) {
             ok = false;
             break;
           }
-          tc_fence_after();
           ok = issue_s(j + 2);
         }
       }
@@ -611,54 +643,65 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     tc_fence_after();
     const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
-    const int esz = p.out_dtype == NVM_F32 ? 4 : 2;
-    const int row_bytes = kD * esz;               // 256 or 512
-    const int chunks = row_bytes / 16;            // 16-byte chunks per row
-    uint8_t* stage = sK;                          // the K/V ring is free once every MMA is done
-    uint8_t* srow = stage + row * row_bytes;
+    // O rows -> shared memory in the TMA store's 128B-swizzled box layout: the tile is
+    // split into boxes of 128 bytes of columns (32 fp32 or 64 16-bit values) x 128 rows,
+    // 16 KB each; row r's 16-byte chunk c of a box sits at r * 128 + ((c ^ (r & 7)) << 4).
+    // The K/V ring is free once every MMA is done.
+    const bool f32_out = p.out_dtype == NVM_F32;
+    uint8_t* srow = sK + row * 128;
+    // two 32-column TMEM loads in flight per wait
 #pragma unroll 1
-    for (int c = 0; c < kD / 32; ++c) {
-      float ov[32];
+    for (int c1 = 0; c1 < kD; c1 += 64) {
+      float ov2[64];
       if (n_tiles > 0) {
-        tmem_ld32(tO + lane_base + c * 32, ov);
+        tmem_ld32(tO + lane_base + c1, *reinterpret_cast<float(*)[32]>(&ov2[0]));
+        tmem_ld32(tO + lane_base + c1 + 32, *reinterpret_cast<float(*)[32]>(&ov2[32]));
         tmem_wait_ld();
       } else {
 #pragma unroll
-        for (int x = 0; x < 32; ++x) ov[x] = 0.f;
+        for (int x = 0; x < 64; ++x) ov2[x] = 0.f;
       }
-      // 32 values = 8 (fp32) or 4 (16-bit) chunks of 16 bytes, chunk index XOR row%8
 #pragma unroll
-      for (int x = 0; x < 32; x += (16 / 4)) {
-        if (esz == 4) {
-          const int ch = (c * 32 + x) / 4;
-          *reinterpret_cast<float4*>(srow + ((ch ^ (row & 7)) << 4)) =
-              make_float4(ov[x] * inv, ov[x + 1] * inv, ov[x + 2] * inv, ov[x + 3] * inv);
-        }
-      }
-      if (esz == 2) {
+      for (int h = 0; h < 2; ++h) {
+        const int c0 = c1 + 32 * h;
+        const float* ov = ov2 + 32 * h;
+        if (f32_out) {
+          uint8_t* box = srow + (c0 / 32) * (kBM * 128);
 #pragma unroll
-        for (int x = 0; x < 32; x += 8) {
-          const int ch = (c * 32 + x) / 8;
-          uint4 v4;
-          if (p.out_dtype == NVM_BF16) {
-            v4 = make_uint4(pack2<__nv_bfloat16>(ov[x] * inv, ov[x + 1] * inv),
-                            pack2<__nv_bfloat16>(ov[x + 2] * inv, ov[x + 3] * inv),
-                            pack2<__nv_bfloat16>(ov[x + 4] * inv, ov[x + 5] * inv),
-                            pack2<__nv_bfloat16>(ov[x + 6] * inv, ov[x + 7] * inv));
-          } else {
-            v4 = make_uint4(pack2<__half>(ov[x] * inv, ov[x + 1] * inv), pack2<__half>(ov[x + 2] * inv, ov[x + 3] * inv),
-                            pack2<__half>(ov[x + 4] * inv, ov[x + 5] * inv), pack2<__half>(ov[x + 6] * inv, ov[x + 7] * inv));
+          for (int x = 0; x < 8; ++x)
+            *reinterpret_cast<float4*>(box + ((x ^ (row & 7)) << 4)) =
+                make_float4(ov[4 * x] * inv, ov[4 * x + 1] * inv, ov[4 * x + 2] * inv, ov[4 * x + 3] * inv);
+        } else {
+          uint8_t* box = srow + (c0 / 64) * (kBM * 128);
+          const int ch0 = (c0 % 64) / 8;
+#pragma unroll
+          for (int x = 0; x < 4; ++x) {
+            uint4 v4;
+            if (p.out_dtype == NVM_BF16) {
+              v4 = make_uint4(cvt_pack<__nv_bfloat16>(ov[8 * x] * inv, ov[8 * x + 1] * inv),
+                              cvt_pack<__nv_bfloat16>(ov[8 * x + 2] * inv, ov[8 * x + 3] * inv),
+                              cvt_pack<__nv_bfloat16>(ov[8 * x + 4] * inv, ov[8 * x + 5] * inv),
+                              cvt_pack<__nv_bfloat16>(ov[8 * x + 6] * inv, ov[8 * x + 7] * inv));
+            } else {
+              v4 = make_uint4(cvt_pack<__half>(ov[8 * x] * inv, ov[8 * x + 1] * inv),
+                              cvt_pack<__half>(ov[8 * x + 2] * inv, ov[8 * x + 3] * inv),
+                              cvt_pack<__half>(ov[8 * x + 4] * inv, ov[8 * x + 5] * inv),
+                              cvt_pack<__half>(ov[8 * x + 6] * inv, ov[8 * x + 7] * inv));
+            }
+            *reinterpret_cast<uint4*>(box + (((ch0 + x) ^ (row & 7)) << 4)) = v4;
           }
-          *reinterpret_cast<uint4*>(srow + ((ch ^ (row & 7)) << 4)) = v4;
         }
       }
     }
+    fence_async_smem();  // generic-proxy stores -> visible to the TMA engine
     named_barrier(1, 128);
-    uint8_t* gout = reinterpret_cast<uint8_t*>(p.out) + (n * p.L + l0) * (int64_t)row_bytes;
-    for (int idx = row; idx < (int)rows * chunks; idx += 128) {
-      const int r = idx / chunks, ch = idx % chunks;
-      *reinterpret_cast<uint4*>(gout + (int64_t)r * row_bytes + ch * 16) =
-          *reinterpret_cast<const uint4*>(stage + r * row_bytes + ((ch ^ (r & 7)) << 4));
+    if (row == 0) {
+      // Rows past L in the last row tile fall outside the tensor map and are not written.
+      const int cols_per_box = f32_out ? 32 : 64;
+      for (int bx = 0; bx < kD / cols_per_box; ++bx)
+        tma_store_3d(&tm_o, sK + bx * (kBM * 128), bx * cols_per_box, (int)l0, (int)n);
+      bulk_commit();
+      bulk_wait_read_all();
     }
   }
 
@@ -677,7 +720,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 // One opt-in to the dynamic shared memory size per kernel instantiation and device.
 template <typename T>
 int launch_typed(dim3 grid, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
-                 const Sm100Params& p, cudaStream_t s) {
+                 const CUtensorMap& to, const Sm100Params& p, cudaStream_t s) {
   static std::mutex mu;
   static uint64_t done = 0;
   int dev = 0;
@@ -692,7 +735,7 @@ int launch_typed(dim3 grid, const CUtensorMap& tq, const CUtensorMap& tk, const 
       done |= 1ull << dev;
     }
   }
-  flash_sm100_kernel<T><<<grid, kThreads, kSmemBytes, s>>>(tq, tk, tv, p);
+  flash_sm100_kernel<T><<<grid, kThreads, kSmemBytes, s>>>(tq, tk, tv, to, p);
   return check_cuda(cudaGetLastError(), "flash_attention: sm100 kernel launch");
 }
 
@@ -711,7 +754,8 @@ bool sm100_prefill_eligible(const PagedArgs& a) {
   }
   if (a.P <= 0 || a.P >= INT32_MAX || a.B * a.Hq > INT32_MAX) return false;
   auto al16 = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
-  return al16(a.q) && al16(a.k_pages) && al16(a.v_pages);
+  if (a.out_dtype != NVM_F32 && a.out_dtype != NVM_F16 && a.out_dtype != NVM_BF16) return false;
+  return al16(a.q) && al16(a.k_pages) && al16(a.v_pages) && al16(a.out);
 }
 
 int launch_sm100_prefill(const PagedArgs& a, cudaStream_t s) {
@@ -732,6 +776,19 @@ int launch_sm100_prefill(const PagedArgs& a, cudaStream_t s) {
   if (st != NVM_OK) return st;
   st = encode_tmap(&tv, dt, 4, a.v_pages, kd, ks, kb, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != NVM_OK) return st;
+  // out [B*Hq, L, D] -> (D, L, B*Hq), boxes of 128 bytes of columns x 128 rows
+  CUtensorMap to;
+  {
+    const int esz = a.out_dtype == NVM_F32 ? 4 : 2;
+    const CUtensorMapDataType odt = a.out_dtype == NVM_F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                    : a.out_dtype == NVM_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                             : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    const uint64_t od[3] = {(uint64_t)kD, (uint64_t)a.L, (uint64_t)(a.B * a.Hq)};
+    const uint64_t os[2] = {(uint64_t)kD * esz, (uint64_t)a.L * kD * esz};
+    const uint32_t ob[3] = {(uint32_t)(128 / esz), (uint32_t)kBM, 1u};
+    st = encode_tmap(&to, odt, 3, a.out, od, os, ob, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st != NVM_OK) return st;
+  }
 
   Sm100Params p{};
   p.out = a.out; p.block_table = a.block_table; p.context_lens = a.context_lens; p.err = device_error_word();
@@ -747,7 +804,7 @@ int launch_sm100_prefill(const PagedArgs& a, cudaStream_t s) {
   }
 
   const dim3 grid((unsigned)(a.B * a.Hq * p.n_row_tiles));
-  if (a.kv_dtype == NVM_F16) return launch_typed<__half>(grid, tq, tk, tv, p, s);
-  return launch_typed<__nv_bfloat16>(grid, tq, tk, tv, p, s);
+  if (a.kv_dtype == NVM_F16) return launch_typed<__half>(grid, tq, tk, tv, to, p, s);
+  return launch_typed<__nv_bfloat16>(grid, tq, tk, tv, to, p, s);
 }
 }  // namespace nvm

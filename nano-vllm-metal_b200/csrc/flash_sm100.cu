@@ -51,6 +51,14 @@ static_assert(kRingBytes >= kBM * kD * 4, "the epilogue stages a 128 x 128 fp32 
 // than this (few-key rows are where one bf16 P rounding shows in the output).
 constexpr int64_t kSplitBelowKeys = 256;
 constexpr float kRescaleThreshold = 8.0f;  // log2(256)
+// Split-K tickets: a fixed region at the start of the workspace (one int per unit).
+constexpr size_t kSm100CounterBytes = 1u << 20;
+
+int64_t env_int(const char* name, int64_t dflt) {
+  const char* v = std::getenv(name);
+  if (v == nullptr || v[0] == '\0') return dflt;
+  return std::atoll(v);
+}
 
 struct Sm100Params {
   void* out;
@@ -65,6 +73,19 @@ struct Sm100Params {
   int dense;
   int box_rows;   // rows of one K/V TMA box: 16 (pages) or kBN (dense)
   int64_t split_below;  // split bf16 P into hi + lo when the tile's first row sees fewer keys
+  // Row units.  Prefill: a unit is the L rows of one q head (Q viewed as [B*Hq, L, D]).
+  // Grouped (few query rows per head): a unit is the g*L rows of one kv head's query
+  // group, which are contiguous in Q (viewed as [B*Hkv, g*L, D]); row r is q head
+  // kvh*g + r/L at position l = r % L.
+  int grouped;
+  int64_t g, M_rows, n_outer, n_units;  // n_units = n_outer * n_row_tiles
+  // Split-K over keys (grouped paged calls): chunk c of a unit covers 64-key tiles
+  // [c*ct, (c+1)*ct); each chunk leaves (m, l) and unnormalised O rows in the workspace
+  // and the unit's last chunk (atomic ticket) merges them.
+  int64_t ct, n_chunks, rows_real;
+  int* counters;
+  float2* part_ml;  // [n_units][n_chunks][rows_real]
+  float* part_o;    // [n_units][n_chunks][rows_real][kD]
 };
 
 __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
@@ -261,23 +282,34 @@ __global__ void __launch_bounds__(kThreads, 2)
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // Chunk-major: every unit's chunk 0 is scheduled before any chunk 1.
+  const int64_t c = blockIdx.x / p.n_units;
+  const int64_t u = blockIdx.x % p.n_units;
   // heavy (late, causal) row tiles first
-  const int64_t rt = p.n_row_tiles - 1 - (int64_t)(blockIdx.x % p.n_row_tiles);
-  const int64_t n = blockIdx.x / p.n_row_tiles;  // flat (b, q head)
-  const int64_t b = n / p.Hq, qh = n % p.Hq;
-  const int64_t kvh = qh / (p.Hq / p.Hkv);
+  const int64_t rt = p.n_row_tiles - 1 - (u % p.n_row_tiles);
+  const int64_t n = u / p.n_row_tiles;  // flat (b, q head), or (b, kv head) when grouped
+  const int64_t b = p.grouped ? n / p.Hkv : n / p.Hq;
+  const int64_t kvh = p.grouped ? n % p.Hkv : (n % p.Hq) / p.g;
   const int64_t ctx = p.dense ? p.dense_ctx : (int64_t)p.context_lens[b];
   const int64_t cap = p.mp * p.ps;
   const int64_t ctx_limit = ctx < cap ? ctx : cap;
-  const int64_t l0 = rt * kBM;
-  const int64_t rows = (p.L - l0) < kBM ? (p.L - l0) : kBM;
+  const int64_t r0 = rt * kBM;  // first row of the tile inside the unit
+  const int64_t rows = (p.M_rows - r0) < kBM ? (p.M_rows - r0) : kBM;
+  // query positions l = r % L of the tile's rows: the smallest and the largest
+  const bool wraps = rows >= p.L || (r0 % p.L) + rows > p.L;
+  const int64_t l_first = wraps ? 0 : r0 % p.L;
+  const int64_t l_last = wraps ? p.L - 1 : (r0 + rows - 1) % p.L;
   int64_t need = ctx_limit;
   if (p.causal) {
-    const int64_t lim = (l0 + rows - 1) + ctx - p.L + 1;
+    const int64_t lim = l_last + ctx - p.L + 1;
     if (lim < need) need = lim;
   }
   if (ctx <= 0 || need < 0) need = 0;
-  const int n_tiles = (int)((need + kBN - 1) / kBN);
+  const int64_t n_tiles_unit = (need + kBN - 1) / kBN;
+  const int64_t n_chunks_unit = n_tiles_unit > 0 ? (n_tiles_unit + p.ct - 1) / p.ct : 1;
+  if (c >= n_chunks_unit) return;  // nothing of this unit left for this chunk (whole CTA, before any set-up)
+  const int64_t t_begin = c * p.ct;  // first 64-key tile of the chunk
+  const int n_tiles = (int)(n_tiles_unit - t_begin < p.ct ? n_tiles_unit - t_begin : p.ct);
 
   // ---------------------------------------------------------------- producer (warp 4)
   // The whole warp runs the loop (warp-uniform values stay on the uniform datapath) and
@@ -296,8 +328,9 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (prod_leader) {
       mbar_arrive_expect_tx(full, kTileBytes);
       if (p.dense) {
-        tma_load_4d(dst, tm, 0, j * kBN, kvh_i, b_i, full);
-        tma_load_4d(dst + kBN * 128, tm, 64, j * kBN, kvh_i, b_i, full);
+        const int key0 = (int)((t_begin + j) * kBN);
+        tma_load_4d(dst, tm, 0, key0, kvh_i, b_i, full);
+        tma_load_4d(dst + kBN * 128, tm, 64, key0, kvh_i, b_i, full);
       } else {
 #pragma unroll
         for (int g = 0; g < kPagesPerTile; ++g) {
@@ -316,7 +349,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (!p.dense) {
 #pragma unroll
         for (int g = 0; g < kPagesPerTile; ++g) {
-          const int pidx = t * kPagesPerTile + g;
+          const int pidx = (int)(t_begin + t) * kPagesPerTile + g;
           int id = pidx < (int)p.mp ? bt_row[pidx] : -1;
           ids_k[g] = (id < 0 || id >= (int)p.P) ? (int)p.P : id;  // hole: out-of-range page, TMA fills zeros
         }
@@ -361,8 +394,8 @@ __global__ void __launch_bounds__(kThreads, 2)
         prefetch_tmap(&tm_k);
         prefetch_tmap(&tm_v);
         mbar_arrive_expect_tx(q_full, kQBytes);
-        tma_load_3d(sQ, &tm_q, 0, (int)l0, (int)n, q_full);
-        tma_load_3d(sQ + kBM * 128, &tm_q, 64, (int)l0, (int)n, q_full);
+        tma_load_3d(sQ, &tm_q, 0, (int)r0, (int)n, q_full);
+        tma_load_3d(sQ + kBM * 128, &tm_q, 64, (int)r0, (int)n, q_full);
       }
     }
     __syncwarp();
@@ -379,7 +412,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t tO = tmem + 2 * kBN;
-  int64_t min_keys = p.causal ? (l0 + ctx - p.L + 1) : ctx_limit;  // keys seen by the tile's first row
+  int64_t min_keys = p.causal ? (l_first + ctx - p.L + 1) : ctx_limit;  // fewest keys any row of the unit sees
   const bool split = kSplit && min_keys < p.split_below;
 
   if (warp == 4) {
@@ -501,10 +534,10 @@ __global__ void __launch_bounds__(kThreads, 2)
     // ---------------------------------------------------------------- softmax warps 0-3
     const int row = warp * 32 + lane;            // TMEM lane == query row in the tile
     const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-    const int64_t lrow = l0 + row;               // query index
-    // last key this row may see: inside the context and, when causal, key <= row + ctx - L
+    const int64_t lpos = (r0 + row) % p.L;       // the row's position among the L query tokens
+    // last key this row may see: inside the context and, when causal, key <= l + ctx - L
     int64_t last_key = ctx_limit - 1;
-    if (p.causal && lrow + ctx - p.L < last_key) last_key = lrow + ctx - p.L;
+    if (p.causal && lpos + ctx - p.L < last_key) last_key = lpos + ctx - p.L;
     if (row >= rows) last_key = -1;
     const float sl2 = p.scale_log2;  // > 0, so max(s) * sl2 == max(s * sl2)
     float m = -INFINITY, lsum = 0.f;  // running max (log2 units, lazily updated) and sum
@@ -520,7 +553,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
       for (int c = 0; c < kBN / 32; ++c) tmem_ld32(tS + c * 32, *reinterpret_cast<float(*)[32]>(&sv[c * 32]));
       tmem_wait_ld();
-      const int64_t key0 = (int64_t)j * kBN;
+      const int64_t key0 = (t_begin + j) * kBN;
       // Only tiles that cross some row's last visible key (the causal diagonal, the
       // context end, rows past L) pay for the mask: one compare per score.
       const int64_t vis64 = last_key - key0;  // in-tile index of the row's last visible key
@@ -642,66 +675,131 @@ __global__ void __launch_bounds__(kThreads, 2)
       *(volatile int*)abort_flag = 1;
     }
     tc_fence_after();
-    const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
     // O rows -> shared memory in the TMA store's 128B-swizzled box layout: the tile is
     // split into boxes of 128 bytes of columns (32 fp32 or 64 16-bit values) x 128 rows,
     // 16 KB each; row r's 16-byte chunk c of a box sits at r * 128 + ((c ^ (r & 7)) << 4).
     // The K/V ring is free once every MMA is done.
     const bool f32_out = p.out_dtype == NVM_F32;
     uint8_t* srow = sK + row * 128;
-    // two 32-column TMEM loads in flight per wait
+    // 32 values of this row (columns c0 .. c0+31), times inv, into the staging boxes
+    auto stage32 = [&](const float* ov, int c0, float inv) {
+      if (f32_out) {
+        uint8_t* box = srow + (c0 / 32) * (kBM * 128);
+#pragma unroll
+        for (int x = 0; x < 8; ++x)
+          *reinterpret_cast<float4*>(box + ((x ^ (row & 7)) << 4)) =
+              make_float4(ov[4 * x] * inv, ov[4 * x + 1] * inv, ov[4 * x + 2] * inv, ov[4 * x + 3] * inv);
+      } else {
+        uint8_t* box = srow + (c0 / 64) * (kBM * 128);
+        const int ch0 = (c0 % 64) / 8;
+#pragma unroll
+        for (int x = 0; x < 4; ++x) {
+          uint4 v4;
+          if (p.out_dtype == NVM_BF16) {
+            v4 = make_uint4(cvt_pack<__nv_bfloat16>(ov[8 * x] * inv, ov[8 * x + 1] * inv),
+                            cvt_pack<__nv_bfloat16>(ov[8 * x + 2] * inv, ov[8 * x + 3] * inv),
+                            cvt_pack<__nv_bfloat16>(ov[8 * x + 4] * inv, ov[8 * x + 5] * inv),
+                            cvt_pack<__nv_bfloat16>(ov[8 * x + 6] * inv, ov[8 * x + 7] * inv));
+          } else {
+            v4 = make_uint4(cvt_pack<__half>(ov[8 * x] * inv, ov[8 * x + 1] * inv),
+                            cvt_pack<__half>(ov[8 * x + 2] * inv, ov[8 * x + 3] * inv),
+                            cvt_pack<__half>(ov[8 * x + 4] * inv, ov[8 * x + 5] * inv),
+                            cvt_pack<__half>(ov[8 * x + 6] * inv, ov[8 * x + 7] * inv));
+          }
+          *reinterpret_cast<uint4*>(box + (((ch0 + x) ^ (row & 7)) << 4)) = v4;
+        }
+      }
+    };
+    bool store = true;
+    if (n_chunks_unit == 1) {
+      const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+      // two 32-column TMEM loads in flight per wait
 #pragma unroll 1
-    for (int c1 = 0; c1 < kD; c1 += 64) {
-      float ov2[64];
-      if (n_tiles > 0) {
+      for (int c1 = 0; c1 < kD; c1 += 64) {
+        float ov2[64];
+        if (n_tiles > 0) {
+          tmem_ld32(tO + lane_base + c1, *reinterpret_cast<float(*)[32]>(&ov2[0]));
+          tmem_ld32(tO + lane_base + c1 + 32, *reinterpret_cast<float(*)[32]>(&ov2[32]));
+          tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int x = 0; x < 64; ++x) ov2[x] = 0.f;
+        }
+        stage32(ov2, c1, inv);
+        stage32(ov2 + 32, c1 + 32, inv);
+      }
+    } else {
+      // Split-K: leave this chunk's (m, l) and unnormalised O rows in the workspace ...
+      const int64_t prow = (u * p.n_chunks + c) * p.rows_real + row;
+      if (row < rows) p.part_ml[prow] = make_float2(m, lsum);  // m = -inf: no visible key in this chunk
+#pragma unroll 1
+      for (int c1 = 0; c1 < kD; c1 += 64) {
+        float ov2[64];
         tmem_ld32(tO + lane_base + c1, *reinterpret_cast<float(*)[32]>(&ov2[0]));
         tmem_ld32(tO + lane_base + c1 + 32, *reinterpret_cast<float(*)[32]>(&ov2[32]));
         tmem_wait_ld();
-      } else {
+        if (row < rows) {
+          float4* po = reinterpret_cast<float4*>(p.part_o + prow * kD + c1);
 #pragma unroll
-        for (int x = 0; x < 64; ++x) ov2[x] = 0.f;
-      }
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int c0 = c1 + 32 * h;
-        const float* ov = ov2 + 32 * h;
-        if (f32_out) {
-          uint8_t* box = srow + (c0 / 32) * (kBM * 128);
-#pragma unroll
-          for (int x = 0; x < 8; ++x)
-            *reinterpret_cast<float4*>(box + ((x ^ (row & 7)) << 4)) =
-                make_float4(ov[4 * x] * inv, ov[4 * x + 1] * inv, ov[4 * x + 2] * inv, ov[4 * x + 3] * inv);
-        } else {
-          uint8_t* box = srow + (c0 / 64) * (kBM * 128);
-          const int ch0 = (c0 % 64) / 8;
-#pragma unroll
-          for (int x = 0; x < 4; ++x) {
-            uint4 v4;
-            if (p.out_dtype == NVM_BF16) {
-              v4 = make_uint4(cvt_pack<__nv_bfloat16>(ov[8 * x] * inv, ov[8 * x + 1] * inv),
-                              cvt_pack<__nv_bfloat16>(ov[8 * x + 2] * inv, ov[8 * x + 3] * inv),
-                              cvt_pack<__nv_bfloat16>(ov[8 * x + 4] * inv, ov[8 * x + 5] * inv),
-                              cvt_pack<__nv_bfloat16>(ov[8 * x + 6] * inv, ov[8 * x + 7] * inv));
-            } else {
-              v4 = make_uint4(cvt_pack<__half>(ov[8 * x] * inv, ov[8 * x + 1] * inv),
-                              cvt_pack<__half>(ov[8 * x + 2] * inv, ov[8 * x + 3] * inv),
-                              cvt_pack<__half>(ov[8 * x + 4] * inv, ov[8 * x + 5] * inv),
-                              cvt_pack<__half>(ov[8 * x + 6] * inv, ov[8 * x + 7] * inv));
-            }
-            *reinterpret_cast<uint4*>(box + (((ch0 + x) ^ (row & 7)) << 4)) = v4;
-          }
+          for (int x = 0; x < 16; ++x) po[x] = make_float4(ov2[4 * x], ov2[4 * x + 1], ov2[4 * x + 2], ov2[4 * x + 3]);
         }
       }
+      // ... and the unit's last chunk to finish merges them (log-sum-exp weights).
+      __threadfence();
+      named_barrier(1, 128);
+      int* last_flag = reinterpret_cast<int*>(tmem_slot + 2);
+      if (row == 0) *(volatile int*)last_flag = atomicAdd(&p.counters[u], 1) == (int)n_chunks_unit - 1;
+      named_barrier(1, 128);
+      store = *(volatile int*)last_flag != 0;
+      if (store) {
+        __threadfence();
+        const int64_t base = u * p.n_chunks * p.rows_real + row;  // + cc * rows_real
+        float mx = -INFINITY, lt = 0.f;
+        if (row < rows) {
+          for (int64_t cc = 0; cc < n_chunks_unit; ++cc) mx = fmaxf(mx, __ldcg(&p.part_ml[base + cc * p.rows_real]).x);
+          for (int64_t cc = 0; cc < n_chunks_unit; ++cc) {
+            const float2 ml = __ldcg(&p.part_ml[base + cc * p.rows_real]);
+            if (ml.x != -INFINITY) lt += ml.y * exp2f(ml.x - mx);
+          }
+        }
+        const float inv = lt > 0.f ? 1.f / lt : 0.f;
+#pragma unroll 1
+        for (int c0 = 0; c0 < kD; c0 += 32) {
+          float acc[32];
+#pragma unroll
+          for (int x = 0; x < 32; ++x) acc[x] = 0.f;
+          if (row < rows) {
+            for (int64_t cc = 0; cc < n_chunks_unit; ++cc) {
+              const float2 ml = __ldcg(&p.part_ml[base + cc * p.rows_real]);
+              if (ml.x == -INFINITY) continue;
+              const float w = exp2f(ml.x - mx);
+              const float4* po = reinterpret_cast<const float4*>(p.part_o + (base + cc * p.rows_real) * kD + c0);
+#pragma unroll
+              for (int x = 0; x < 8; ++x) {
+                const float4 o4 = __ldcg(po + x);
+                acc[4 * x] += w * o4.x;
+                acc[4 * x + 1] += w * o4.y;
+                acc[4 * x + 2] += w * o4.z;
+                acc[4 * x + 3] += w * o4.w;
+              }
+            }
+          }
+          stage32(acc, c0, inv);
+        }
+        if (row == 0) p.counters[u] = 0;  // tickets start at zero for the next call
+      }
     }
-    fence_async_smem();  // generic-proxy stores -> visible to the TMA engine
-    named_barrier(1, 128);
-    if (row == 0) {
-      // Rows past L in the last row tile fall outside the tensor map and are not written.
-      const int cols_per_box = f32_out ? 32 : 64;
-      for (int bx = 0; bx < kD / cols_per_box; ++bx)
-        tma_store_3d(&tm_o, sK + bx * (kBM * 128), bx * cols_per_box, (int)l0, (int)n);
-      bulk_commit();
-      bulk_wait_read_all();
+    if (store) {
+      fence_async_smem();  // generic-proxy stores -> visible to the TMA engine
+      named_barrier(1, 128);
+      if (row == 0) {
+        // Rows past the unit's end fall outside the tensor map and are not written.
+        const int cols_per_box = f32_out ? 32 : 64;
+        for (int bx = 0; bx < kD / cols_per_box; ++bx)
+          tma_store_3d(&tm_o, sK + bx * (kBM * 128), bx * cols_per_box, (int)r0, (int)n);
+        bulk_commit();
+        bulk_wait_read_all();
+      }
     }
   }
 
@@ -741,28 +839,78 @@ int launch_typed(dim3 grid, const CUtensorMap& tq, const CUtensorMap& tk, const 
 
 }  // namespace
 
-bool sm100_prefill_eligible(const PagedArgs& a) {
-  if (a.kv_dtype != NVM_F16 && a.kv_dtype != NVM_BF16) return false;
-  if (a.q_dtype != a.kv_dtype) return false;
-  if (a.D != kD) return false;
-  if (a.L < 64) return false;
-  if (!(a.scale > 0.f)) return false;  // the softmax takes row maxima before scaling
+Sm100Plan plan_sm100(const PagedArgs& a, bool sizing_only) {
+  Sm100Plan plan{};
+  plan.eligible = false;
+  if (a.kv_dtype != NVM_F16 && a.kv_dtype != NVM_BF16) return plan;
+  if (!sizing_only && a.q_dtype != a.kv_dtype) return plan;
+  if (a.D != kD) return plan;
+  if (!sizing_only && !(a.scale > 0.f)) return plan;  // the softmax takes row maxima before scaling
   if (a.dense) {
-    if (a.page_size < kBN) return false;  // dense boxes are kBN rows
+    if (a.page_size < kBN) return plan;  // dense boxes are kBN rows
   } else if (a.page_size != 16) {
-    return false;
+    return plan;
   }
-  if (a.P <= 0 || a.P >= INT32_MAX || a.B * a.Hq > INT32_MAX) return false;
-  auto al16 = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
-  if (a.out_dtype != NVM_F32 && a.out_dtype != NVM_F16 && a.out_dtype != NVM_BF16) return false;
-  return al16(a.q) && al16(a.k_pages) && al16(a.v_pages) && al16(a.out);
+  if (a.P <= 0 || a.P >= INT32_MAX || a.B * a.Hq > INT32_MAX) return plan;
+  if (!sizing_only) {
+    auto al16 = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
+    if (a.out_dtype != NVM_F32 && a.out_dtype != NVM_F16 && a.out_dtype != NVM_BF16) return plan;
+    if (!(al16(a.q) && al16(a.k_pages) && al16(a.v_pages) && al16(a.out))) return plan;
+  }
+  const int64_t g = a.Hq / a.Hkv;
+  // Prefill: >= 64 query rows per head.  Grouped: 2..63 query tokens with >= 16 rows per
+  // kv head (g*L); fewer rows stay on the mma.sync decode kernel, which is HBM-bound there.
+  const int64_t min_rows = env_int("NVM_SM100_GROUPED_MIN_ROWS", 16);
+  if (a.L >= 64) {
+    plan.grouped = 0;
+    plan.M_rows = a.L;
+    plan.n_outer = a.B * a.Hq;
+  } else if (a.L > 1 && g * a.L >= min_rows && env_int("NVM_SM100_GROUPED", 1) != 0) {
+    plan.grouped = 1;
+    plan.M_rows = g * a.L;
+    plan.n_outer = a.B * a.Hkv;
+  } else {
+    return plan;
+  }
+  plan.n_row_tiles = (plan.M_rows + kBM - 1) / kBM;
+  plan.n_units = plan.n_outer * plan.n_row_tiles;
+  plan.rows_real = plan.M_rows < kBM ? plan.M_rows : kBM;
+  const int64_t keys = a.dense ? a.page_size : a.max_pages * a.page_size;
+  const int64_t tiles_max = (keys + kBN - 1) / kBN;
+  plan.ct = tiles_max > 0 ? tiles_max : 1;
+  plan.n_chunks = 1;
+  // Split-K over keys for grouped paged calls (dense callers pass no workspace): aim at
+  // a few CTAs per SM slot if every sequence were max_pages long; units whose context is
+  // shorter leave their later chunks empty (those CTAs return at once).
+  if (plan.grouped && !a.dense && plan.n_units <= (int64_t)(kSm100CounterBytes / sizeof(int))) {
+    int64_t ct = env_int("NVM_SM100_CHUNK_TILES", 0);
+    if (ct <= 0) {
+      const int64_t target = 148 * 2 * 4;
+      ct = (plan.n_units * tiles_max + target - 1) / target;
+      if (ct < 8) ct = 8;
+    }
+    if (ct < tiles_max) {
+      plan.ct = ct;
+      plan.n_chunks = (tiles_max + ct - 1) / ct;
+    }
+  }
+  if (plan.n_units * plan.n_chunks > INT32_MAX) return plan;
+  plan.ws_bytes = 0;
+  if (plan.n_chunks > 1) {
+    const size_t ml = (size_t)(plan.n_units * plan.n_chunks * plan.rows_real) * sizeof(float2);
+    plan.ws_bytes = kSm100CounterBytes + ((ml + 255) & ~size_t(255)) +
+                    (size_t)(plan.n_units * plan.n_chunks * plan.rows_real) * kD * sizeof(float);
+  }
+  plan.eligible = true;
+  return plan;
 }
 
-int launch_sm100_prefill(const PagedArgs& a, cudaStream_t s) {
+int launch_sm100(const PagedArgs& a, const Sm100Plan& plan, void* ws, cudaStream_t s) {
   const CUtensorMapDataType dt = a.kv_dtype == NVM_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-  // Q [B*Hq, L, D] -> (D, L, B*Hq), 64 x 128 boxes
-  const uint64_t qd[3] = {(uint64_t)kD, (uint64_t)a.L, (uint64_t)(a.B * a.Hq)};
-  const uint64_t qs[2] = {kD * 2, (uint64_t)a.L * kD * 2};
+  // Q as [n_outer, M_rows, D] -> (D, M_rows, n_outer), 64 x 128 boxes (rows past a unit's end are
+  // outside the map and load as zeros)
+  const uint64_t qd[3] = {(uint64_t)kD, (uint64_t)plan.M_rows, (uint64_t)plan.n_outer};
+  const uint64_t qs[2] = {kD * 2, (uint64_t)plan.M_rows * kD * 2};
   const uint32_t qb[3] = {64u, (uint32_t)kBM, 1u};
   CUtensorMap tq, tk, tv;
   int st = encode_tmap(&tq, dt, 3, a.q, qd, qs, qb, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -776,15 +924,15 @@ int launch_sm100_prefill(const PagedArgs& a, cudaStream_t s) {
   if (st != NVM_OK) return st;
   st = encode_tmap(&tv, dt, 4, a.v_pages, kd, ks, kb, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != NVM_OK) return st;
-  // out [B*Hq, L, D] -> (D, L, B*Hq), boxes of 128 bytes of columns x 128 rows
+  // out, same [n_outer, M_rows, D] view, boxes of 128 bytes of columns x 128 rows
   CUtensorMap to;
   {
     const int esz = a.out_dtype == NVM_F32 ? 4 : 2;
     const CUtensorMapDataType odt = a.out_dtype == NVM_F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                                     : a.out_dtype == NVM_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                                              : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-    const uint64_t od[3] = {(uint64_t)kD, (uint64_t)a.L, (uint64_t)(a.B * a.Hq)};
-    const uint64_t os[2] = {(uint64_t)kD * esz, (uint64_t)a.L * kD * esz};
+    const uint64_t od[3] = {(uint64_t)kD, (uint64_t)plan.M_rows, (uint64_t)plan.n_outer};
+    const uint64_t os[2] = {(uint64_t)kD * esz, (uint64_t)plan.M_rows * kD * esz};
     const uint32_t ob[3] = {(uint32_t)(128 / esz), (uint32_t)kBM, 1u};
     st = encode_tmap(&to, odt, 3, a.out, od, os, ob, CU_TENSOR_MAP_SWIZZLE_128B);
     if (st != NVM_OK) return st;
@@ -795,15 +943,25 @@ int launch_sm100_prefill(const PagedArgs& a, cudaStream_t s) {
   p.out_dtype = a.out_dtype;
   p.B = a.B; p.Hq = a.Hq; p.Hkv = a.Hkv; p.L = a.L; p.P = a.P; p.ps = a.page_size; p.mp = a.max_pages;
   p.dense_ctx = a.dense_ctx;
-  p.n_row_tiles = (a.L + kBM - 1) / kBM;
+  p.n_row_tiles = plan.n_row_tiles;
   p.scale_log2 = a.scale * 1.4426950408889634f;
   p.causal = a.is_causal; p.dense = a.dense; p.box_rows = box_rows;
-  {
-    const char* e = std::getenv("NVM_SM100_SPLIT_BELOW");  // tuning: 0 = never split, huge = always
-    p.split_below = (e != nullptr && e[0] != '\0') ? std::atoll(e) : kSplitBelowKeys;
+  p.split_below = env_int("NVM_SM100_SPLIT_BELOW", kSplitBelowKeys);  // tuning: 0 = never, huge = always
+  p.grouped = plan.grouped;
+  p.g = a.Hq / a.Hkv;
+  p.M_rows = plan.M_rows; p.n_outer = plan.n_outer; p.n_units = plan.n_units;
+  p.ct = plan.ct; p.n_chunks = plan.n_chunks; p.rows_real = plan.rows_real;
+  if (plan.n_chunks > 1) {
+    uint8_t* w = static_cast<uint8_t*>(ws);
+    p.counters = reinterpret_cast<int*>(w);
+    w += kSm100CounterBytes;
+    p.part_ml = reinterpret_cast<float2*>(w);
+    const size_t ml = (size_t)(plan.n_units * plan.n_chunks * plan.rows_real) * sizeof(float2);
+    w += (ml + 255) & ~size_t(255);
+    p.part_o = reinterpret_cast<float*>(w);
   }
 
-  const dim3 grid((unsigned)(a.B * a.Hq * p.n_row_tiles));
+  const dim3 grid((unsigned)(plan.n_units * plan.n_chunks));
   if (a.kv_dtype == NVM_F16) return launch_typed<__half>(grid, tq, tk, tv, to, p, s);
   return launch_typed<__nv_bfloat16>(grid, tq, tk, tv, to, p, s);
 }

@@ -181,8 +181,15 @@ size_t nvm_paged_attention_workspace_size(int64_t B, int64_t Hq, int64_t Hkv, in
   a.is_causal = 1;
   if (validate_paged(a, false) != NVM_OK) return 0;
   if (env_flag("NVM_ATTN_FORCE_GENERIC")) return 0;
+  // q's dtype is not known here: cover the tcgen05 plan (taken when q matches the pages)
+  // and the mma.sync plan (taken otherwise).
   MmaPlan plan = plan_paged_mma(a);
-  return plan.eligible ? plan.ws_bytes : 0;
+  size_t need = plan.eligible ? plan.ws_bytes : 0;
+  if (!env_flag("NVM_ATTN_NO_SM100")) {
+    const Sm100Plan sp = plan_sm100(a, true);
+    if (sp.eligible && sp.ws_bytes > need) need = sp.ws_bytes;
+  }
+  return need;
 }
 
 int nvm_paged_attention(const void* q, int q_dtype, const void* k_pages, const void* v_pages, int kv_dtype,
@@ -202,7 +209,15 @@ int nvm_paged_attention(const void* q, int q_dtype, const void* k_pages, const v
   if (B == 0) return NVM_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (!env_flag("NVM_ATTN_FORCE_GENERIC")) {
-    if (!env_flag("NVM_ATTN_NO_SM100") && sm100_prefill_eligible(a)) return launch_sm100_prefill(a, s);
+    if (!env_flag("NVM_ATTN_NO_SM100")) {
+      const Sm100Plan sp = plan_sm100(a, false);
+      if (sp.eligible) {
+        if (sp.ws_bytes > 0 && (workspace == nullptr || workspace_bytes < sp.ws_bytes))
+          return fail(NVM_ERR_WORKSPACE, "paged_attention: workspace of %zu bytes required, %zu given", sp.ws_bytes,
+                      workspace_bytes);
+        return launch_sm100(a, sp, workspace, s);
+      }
+    }
     MmaPlan plan = plan_paged_mma(a);
     if (plan.eligible) {
       if (plan.ws_bytes > 0 && (workspace == nullptr || workspace_bytes < plan.ws_bytes))
@@ -235,7 +250,10 @@ int nvm_flash_attention(const void* q, const void* k, const void* v, int dtype, 
     a.block_table = nullptr; a.context_lens = nullptr; a.out = out; a.out_dtype = out_dtype;
     a.B = B; a.Hq = Hq; a.Hkv = Hkv; a.L = L; a.D = D; a.P = B; a.page_size = S; a.max_pages = 1;
     a.scale = scale; a.is_causal = is_causal ? 1 : 0; a.dense = 1; a.dense_ctx = S;
-    if (!env_flag("NVM_ATTN_NO_SM100") && sm100_prefill_eligible(a)) return launch_sm100_prefill(a, s);
+    if (!env_flag("NVM_ATTN_NO_SM100")) {
+      const Sm100Plan sp = plan_sm100(a, false);
+      if (sp.eligible && sp.ws_bytes == 0) return launch_sm100(a, sp, nullptr, s);
+    }
     MmaPlan plan = plan_paged_mma(a);
     if (plan.eligible && plan.ws_bytes == 0) return launch_paged_mma(a, plan, nullptr, s);
   }

@@ -81,8 +81,18 @@ MmaPlan plan_paged_mma(const PagedArgs& a);
 int launch_paged_mma(const PagedArgs& a, const MmaPlan& plan, void* workspace, cudaStream_t s);
 
 // tcgen05 / TMEM causal prefill (dense or paged) for 16-bit Q/K/V, D == 128.
-bool sm100_prefill_eligible(const PagedArgs& a);
-int launch_sm100_prefill(const PagedArgs& a, cudaStream_t s);
+// tcgen05/TMEM kernel (flash_sm100.cu): prefill (>= 64 query rows per head) and grouped
+// few-token calls (a kv head's g*L query rows as one tile, split-K over keys when paged).
+struct Sm100Plan {
+  bool eligible;
+  int grouped;
+  int64_t M_rows, n_outer, n_row_tiles, n_units, rows_real, ct, n_chunks;
+  size_t ws_bytes;
+};
+// sizing_only: plan from shapes alone (q dtype, pointers and scale unknown), for
+// nvm_paged_attention_workspace_size.
+Sm100Plan plan_sm100(const PagedArgs& a, bool sizing_only);
+int launch_sm100(const PagedArgs& a, const Sm100Plan& plan, void* ws, cudaStream_t s);
 
 int launch_kv_write(const void* k, const void* v, int in_dtype, int64_t stride_t, int64_t stride_h,
                     void* k_pages, void* v_pages, int kv_dtype, void* k_scales, void* v_scales,

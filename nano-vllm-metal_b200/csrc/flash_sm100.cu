@@ -45,12 +45,17 @@ constexpr int kQBytes = kBM * kD * 2;     // 32 KB
 constexpr int kRingBytes = (kKStages + kVStages) * kTileBytes;  // 80 KB, also the epilogue's staging area
 constexpr int kThreads = 192;
 constexpr int kTmemCols = 256;   // S0 [0,64), S1 [64,128), O [128,256): two CTAs fit per SM
-constexpr int kSmemBytes = kQBytes + kRingBytes + 256;  // 112.25 KB (+1 KB reserved each): two CTAs per SM
+// Paged calls: one bit per page of the CTA's key chunk, set for holes (the softmax
+// masks them from shared memory instead of re-reading the block table every tile).
+constexpr int kHoleWords = 128;  // 4096 pages = 1024 tiles; longer chunks read the block table
+constexpr int kSmemBytes = kQBytes + kRingBytes + 256 + kHoleWords * 4;  // 112.75 KB (+1 KB reserved each): two CTAs per SM
 static_assert(kRingBytes >= kBM * kD * 4, "the epilogue stages a 128 x 128 fp32 tile in the K/V ring");
 // bf16 P is split into hi + lo operands only for row tiles whose rows see fewer keys
 // than this (few-key rows are where one bf16 P rounding shows in the output).
 constexpr int64_t kSplitBelowKeys = 256;
 constexpr float kRescaleThreshold = 8.0f;  // log2(256)
+// Grouped calls: K/V tiles this far ahead of the one being loaded are prefetched into L2.
+constexpr int kPrefetchTiles = 4;
 // Split-K tickets: a fixed region at the start of the workspace (one int per unit).
 constexpr size_t kSm100CounterBytes = 1u << 20;
 
@@ -83,6 +88,7 @@ struct Sm100Params {
   // [c*ct, (c+1)*ct); each chunk leaves (m, l) and unnormalised O rows in the workspace
   // and the unit's last chunk (atomic ticket) merges them.
   int64_t ct, n_chunks, rows_real;
+  int prefetch;  // grouped calls: prefetch K/V tiles kPrefetchTiles ahead into L2
   int* counters;
   float2* part_ml;  // [n_units][n_chunks][rows_real]
   float* part_o;    // [n_units][n_chunks][rows_real][kD]
@@ -280,6 +286,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint64_t* mma_done = o_done + 1;           // every MMA of the CTA complete (one completion)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+  int* hole_state = abort_flag + 2;  // 0: no holes in the chunk, 1: see hole_bits, 2: read the block table
+  uint32_t* hole_bits = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(bars) + 256);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // Chunk-major: every unit's chunk 0 is scheduled before any chunk 1.
@@ -342,20 +350,70 @@ __global__ void __launch_bounds__(kThreads, 2)
     __syncwarp();
   };
   // loop iteration t: K_t (t < n_tiles) and V_{t-1} (t >= 1); false if a wait expired
+  // Paged calls: the page ids of 8 tiles (32 pages) sit one per lane of the producer
+  // warp and are loaded one 8-tile block ahead, so no block-table read stands in front
+  // of a copy.  Lane i of block blk holds page blk*32 + i of the chunk; holes and pages
+  // past the table read as the out-of-range page P (TMA fills zeros).
+  int id_cur = 0, id_next = 0, id_blk = 0;
+  auto load_ids = [&](int blk) -> int {
+    const int pidx = (int)(t_begin * kPagesPerTile) + blk * 32 + lane;
+    const int id = pidx < (int)p.mp ? bt_row[pidx] : -1;
+    return (id < 0 || id >= (int)p.P) ? (int)p.P : id;
+  };
+  // page g of chunk tile t (t in the current or the next 8-tile block); all 32 lanes call it
+  auto page_id = [&](int t, int g) -> int {
+    const int v_cur = __shfl_sync(0xffffffffu, id_cur, (t % 8) * kPagesPerTile + g);
+    const int v_next = __shfl_sync(0xffffffffu, id_next, (t % 8) * kPagesPerTile + g);
+    return t / 8 == id_blk ? v_cur : v_next;
+  };
   auto produce = [&](int t) -> bool {
     if (t < n_tiles) {
       const int s = t % kKStages;
       if (t >= kKStages && !warp_wait(&k_empty[s], ((t / kKStages) & 1) ^ 1)) return false;
       if (!p.dense) {
-#pragma unroll
-        for (int g = 0; g < kPagesPerTile; ++g) {
-          const int pidx = (int)(t_begin + t) * kPagesPerTile + g;
-          int id = pidx < (int)p.mp ? bt_row[pidx] : -1;
-          ids_k[g] = (id < 0 || id >= (int)p.P) ? (int)p.P : id;  // hole: out-of-range page, TMA fills zeros
+        if (t / 8 != id_blk) {  // entering the next block: shift, and load the one after
+          id_cur = id_next;
+          id_blk = t / 8;
+          id_next = load_ids(id_blk + 1);
         }
+#pragma unroll
+        for (int g = 0; g < kPagesPerTile; ++g) ids_k[g] = page_id(t, g);
       }
       issue(&tm_k, sK + s * kTileBytes, &k_full[s], t, ids_k);
       k_issued = t + 1;
+      // Grouped (decode-like) calls stream K/V from HBM once: the rings are only a few
+      // tiles deep, so tile t + kPrefetchTiles is pulled into L2 now.
+      const int tp = t + kPrefetchTiles;
+      if (p.grouped && p.prefetch && tp < n_tiles) {
+        if (prod_leader) {
+          if (p.dense) {
+            const int key0 = (int)((t_begin + tp) * kBN);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              tma_prefetch_4d(&tm_k, h * 64, key0, kvh_i, b_i);
+              tma_prefetch_4d(&tm_v, h * 64, key0, kvh_i, b_i);
+            }
+          }
+        }
+        if (!p.dense) {
+          int pf[kPagesPerTile];
+#pragma unroll
+          for (int g = 0; g < kPagesPerTile; ++g) pf[g] = page_id(tp, g);
+          if (prod_leader) {
+#pragma unroll
+            for (int g = 0; g < kPagesPerTile; ++g) {
+              if (pf[g] < (int)p.P) {
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                  tma_prefetch_4d(&tm_k, h * 64, 0, kvh_i, pf[g]);
+                  tma_prefetch_4d(&tm_v, h * 64, 0, kvh_i, pf[g]);
+                }
+              }
+            }
+          }
+        }
+        __syncwarp();
+      }
     }
     if (t >= 1) {
       const int j = t - 1, s = j % kVStages;
@@ -399,6 +457,34 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
     }
     __syncwarp();
+    if (!p.dense && n_tiles > 0) {
+      id_cur = load_ids(0);
+      id_next = load_ids(1);
+      // hole bitmask of the chunk's pages (read once, coalesced, before the block barrier)
+      const int n_pages = n_tiles * kPagesPerTile;
+      if (n_pages <= kHoleWords * 32) {
+        uint32_t any = 0;
+        for (int w0 = 0; w0 < n_pages; w0 += 32 * 4) {
+          bool hole[4];
+#pragma unroll
+          for (int x = 0; x < 4; ++x) {
+            const int i = w0 + x * 32 + lane;  // page of the chunk
+            const int pidx = (int)(t_begin * kPagesPerTile) + i;
+            const int id = (i < n_pages && pidx < (int)p.mp) ? bt_row[pidx] : 0;
+            hole[x] = i < n_pages && (pidx >= (int)p.mp || id < 0 || id >= (int)p.P);
+          }
+#pragma unroll
+          for (int x = 0; x < 4; ++x) {
+            const uint32_t bits = __ballot_sync(0xffffffffu, hole[x]);
+            any |= bits;
+            if (lane == 0 && w0 / 32 + x < kHoleWords) hole_bits[w0 / 32 + x] = bits;
+          }
+        }
+        if (lane == 0) *hole_state = any ? 1 : 0;
+      } else if (lane == 0) {
+        *hole_state = 2;
+      }
+    }
     for (; t_next < kKStages && t_next <= n_tiles && n_tiles > 0; ++t_next) produce(t_next);  // no waits
   }
   if (warp == 5) {
@@ -562,7 +648,19 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
         for (int c = 0; c < kBN; ++c) sv[c] = c <= vis ? sv[c] : -INFINITY;
       }
-      if (!p.dense) {  // holes: the 16-token groups of missing pages are masked
+      const int hstate = p.dense ? 0 : *hole_state;
+      if (hstate == 1) {  // holes: the 16-token groups of missing pages are masked
+        const uint32_t bits = (hole_bits[(j * kPagesPerTile) / 32] >> ((j * kPagesPerTile) % 32)) & 0xFu;
+        if (bits != 0) {
+#pragma unroll
+          for (int g = 0; g < kPagesPerTile; ++g) {
+            if ((bits >> g) & 1u) {
+#pragma unroll
+              for (int c = 0; c < 16; ++c) sv[g * 16 + c] = -INFINITY;
+            }
+          }
+        }
+      } else if (hstate == 2) {
 #pragma unroll
         for (int g = 0; g < kBN / 16; ++g) {
           const int64_t pidx = (key0 + g * 16) / p.ps;
@@ -951,6 +1049,7 @@ int launch_sm100(const PagedArgs& a, const Sm100Plan& plan, void* ws, cudaStream
   p.g = a.Hq / a.Hkv;
   p.M_rows = plan.M_rows; p.n_outer = plan.n_outer; p.n_units = plan.n_units;
   p.ct = plan.ct; p.n_chunks = plan.n_chunks; p.rows_real = plan.rows_real;
+  p.prefetch = (int)env_int("NVM_SM100_PREFETCH", 0);
   if (plan.n_chunks > 1) {
     uint8_t* w = static_cast<uint8_t*>(ws);
     p.counters = reinterpret_cast<int*>(w);

@@ -45,19 +45,17 @@ constexpr int kQBytes = kBM * kD * 2;     // 32 KB
 constexpr int kRingBytes = (kKStages + kVStages) * kTileBytes;  // 80 KB, also the epilogue's staging area
 constexpr int kThreads = 192;
 constexpr int kTmemCols = 256;   // S0 [0,64), S1 [64,128), O [128,256): two CTAs fit per SM
-// Paged calls: one bit per page of the CTA's key chunk, set for holes (the softmax
-// masks them from shared memory instead of re-reading the block table every tile).
-constexpr int kHoleWords = 128;  // 4096 pages = 1024 tiles; longer chunks read the block table
-constexpr int kSmemBytes = kQBytes + kRingBytes + 256 + kHoleWords * 4;  // 112.75 KB (+1 KB reserved each): two CTAs per SM
+constexpr int kBarBytes = 512;   // mbarriers, TMEM address, flags, the 4-slot item ring
+constexpr int kSmemBytes = kQBytes + kRingBytes + kBarBytes;  // 112.5 KB (+1 KB reserved each): two CTAs per SM
 static_assert(kRingBytes >= kBM * kD * 4, "the epilogue stages a 128 x 128 fp32 tile in the K/V ring");
 // bf16 P is split into hi + lo operands only for row tiles whose rows see fewer keys
 // than this (few-key rows are where one bf16 P rounding shows in the output).
 constexpr int64_t kSplitBelowKeys = 256;
 constexpr float kRescaleThreshold = 8.0f;  // log2(256)
-// Grouped calls: K/V tiles this far ahead of the one being loaded are prefetched into L2.
-constexpr int kPrefetchTiles = 4;
-// Split-K tickets: a fixed region at the start of the workspace (one int per unit).
+// Split-K tickets: a fixed region at the start of the workspace (one int per unit); its
+// last two ints are the work-item counter and the exit counter of the persistent grid.
 constexpr size_t kSm100CounterBytes = 1u << 20;
+constexpr int64_t kMaxTicketUnits = (int64_t)(kSm100CounterBytes / sizeof(int)) - 2;
 
 int64_t env_int(const char* name, int64_t dflt) {
   const char* v = std::getenv(name);
@@ -88,7 +86,10 @@ struct Sm100Params {
   // [c*ct, (c+1)*ct); each chunk leaves (m, l) and unnormalised O rows in the workspace
   // and the unit's last chunk (atomic ticket) merges them.
   int64_t ct, n_chunks, rows_real;
-  int prefetch;  // grouped calls: prefetch K/V tiles kPrefetchTiles ahead into L2
+  int64_t n_items;    // n_units * n_chunks work items
+  int* work_counter;  // next item (in the workspace); null: item = blockIdx.x + k * gridDim.x
+  int stage_out;      // one item per CTA: O leaves through shared memory and bulk tensor stores
+  int* exit_counter;  // CTAs done; the last one resets both counters
   int* counters;
   float2* part_ml;  // [n_units][n_chunks][rows_real]
   float* part_o;    // [n_units][n_chunks][rows_real][kD]
@@ -260,6 +261,50 @@ __device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t (&r)[3
       : "memory");
 }
 
+// Geometry of one work item (a 128-row tile of a row unit x a chunk of 64-key tiles).
+// Every warp role decodes the same item index to the same values.
+struct Item {
+  int64_t c, u, n, b, kvh, r0, rows, ctx, ctx_limit, l_first, t_begin, n_chunks_unit;
+  int n_tiles;  // 64-key tiles of this item (0: no keys; still produces zero rows when valid)
+  bool valid;   // false: a chunk past the unit's last key (nothing to do)
+};
+
+__device__ __forceinline__ Item decode_item(const Sm100Params& p, int64_t item) {
+  Item it;
+  it.c = item / p.n_units;  // chunk-major: every unit's chunk 0 comes before any chunk 1
+  it.u = item % p.n_units;
+  const int64_t rt = p.n_row_tiles - 1 - (it.u % p.n_row_tiles);  // heavy (late, causal) row tiles first
+  it.n = it.u / p.n_row_tiles;  // flat (b, q head), or (b, kv head) when grouped
+  it.b = p.grouped ? it.n / p.Hkv : it.n / p.Hq;
+  it.kvh = p.grouped ? it.n % p.Hkv : (it.n % p.Hq) / p.g;
+  it.ctx = p.dense ? p.dense_ctx : (int64_t)p.context_lens[it.b];
+  const int64_t cap = p.mp * p.ps;
+  it.ctx_limit = it.ctx < cap ? it.ctx : cap;
+  it.r0 = rt * kBM;  // first row of the tile inside the unit
+  it.rows = (p.M_rows - it.r0) < kBM ? (p.M_rows - it.r0) : kBM;
+  // query positions l = r % L of the tile's rows: the smallest and the largest
+  const bool wraps = it.rows >= p.L || (it.r0 % p.L) + it.rows > p.L;
+  it.l_first = wraps ? 0 : it.r0 % p.L;
+  const int64_t l_last = wraps ? p.L - 1 : (it.r0 + it.rows - 1) % p.L;
+  int64_t need = it.ctx_limit;
+  if (p.causal) {
+    const int64_t lim = l_last + it.ctx - p.L + 1;
+    if (lim < need) need = lim;
+  }
+  if (it.ctx <= 0 || need < 0) need = 0;
+  const int64_t n_tiles_unit = (need + kBN - 1) / kBN;
+  it.n_chunks_unit = n_tiles_unit > 0 ? (n_tiles_unit + p.ct - 1) / p.ct : 1;
+  it.valid = it.c < it.n_chunks_unit;
+  it.t_begin = it.c * p.ct;
+  const int64_t left = n_tiles_unit - it.t_begin;
+  it.n_tiles = it.valid && left > 0 ? (int)(left < p.ct ? left : p.ct) : 0;
+  return it;
+}
+
+// Persistent: each CTA loops over work items (fetched from a counter in the workspace
+// when there is one, else blockIdx.x + k * gridDim.x).  Rings and mbarrier phases run on
+// per-CTA tile counters, so the next item's Q load, K/V loads and first S overlap the
+// previous item's last tiles and epilogue.
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 2)
     flash_sm100_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -275,217 +320,51 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint8_t* sK = smem + kQBytes;             // [kKStages] K tiles
   uint8_t* sV = sK + kKStages * kTileBytes;  // [kVStages] V tiles
   uint64_t* bars = reinterpret_cast<uint64_t*>(sK + kRingBytes);
-  uint64_t* q_full = bars;
-  uint64_t* k_full = q_full + 1;             // [kKStages] K_j landed
-  uint64_t* k_empty = k_full + kKStages;     // [kKStages] S_j has read K_j
-  uint64_t* v_full = k_empty + kKStages;     // [kVStages] V_j landed
-  uint64_t* v_empty = v_full + kVStages;     // [kVStages] PV_j has read V_j
-  uint64_t* s_full = v_empty + kVStages;     // [2] S_j in TMEM buffer j&1
-  uint64_t* p_full = s_full + 2;             // [2] P_j written over S_j (count 128)
-  uint64_t* o_done = p_full + 2;             // PV_j complete
-  uint64_t* mma_done = o_done + 1;           // every MMA of the CTA complete (one completion)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  uint64_t* q_full = bars;                   // Q of the CTA's i-th item with keys landed
+  uint64_t* q_empty = q_full + 1;            // the last S of that item has read Q
+  uint64_t* k_full = q_empty + 1;            // [kKStages] K tile landed
+  uint64_t* k_empty = k_full + kKStages;     // [kKStages] S has read it
+  uint64_t* v_full = k_empty + kKStages;     // [kVStages] V tile landed
+  uint64_t* v_empty = v_full + kVStages;     // [kVStages] PV has read it
+  uint64_t* s_full = v_empty + kVStages;     // [2] S_G in TMEM buffer G&1
+  uint64_t* p_full = s_full + 2;             // [2] P_G written over S_G (count 128)
+  uint64_t* o_done = p_full + 2;             // PV_G complete (one completion per tile)
+  uint64_t* item_done = o_done + 1;          // every PV of an item complete (one per item)
+  uint64_t* o_free = item_done + 1;          // the softmax warps have read an item's O (count 128)
+  uint64_t* mma_done = o_free + 1;           // every MMA of the CTA complete (teardown)
+  uint64_t* item_full = mma_done + 1;        // [4] item index published in item_ring
+  uint64_t* item_empty = item_full + 4;      // [4] read by the MMA warp and the 4 softmax warps
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(item_empty + 4);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
-  int* hole_state = abort_flag + 2;  // 0: no holes in the chunk, 1: see hole_bits, 2: read the block table
-  uint32_t* hole_bits = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(bars) + 256);
+  int* last_flag = abort_flag + 1;
+  int64_t* item_ring = reinterpret_cast<int64_t*>(reinterpret_cast<uint8_t*>(bars) + 256);  // [4]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // Chunk-major: every unit's chunk 0 is scheduled before any chunk 1.
-  const int64_t c = blockIdx.x / p.n_units;
-  const int64_t u = blockIdx.x % p.n_units;
-  // heavy (late, causal) row tiles first
-  const int64_t rt = p.n_row_tiles - 1 - (u % p.n_row_tiles);
-  const int64_t n = u / p.n_row_tiles;  // flat (b, q head), or (b, kv head) when grouped
-  const int64_t b = p.grouped ? n / p.Hkv : n / p.Hq;
-  const int64_t kvh = p.grouped ? n % p.Hkv : (n % p.Hq) / p.g;
-  const int64_t ctx = p.dense ? p.dense_ctx : (int64_t)p.context_lens[b];
-  const int64_t cap = p.mp * p.ps;
-  const int64_t ctx_limit = ctx < cap ? ctx : cap;
-  const int64_t r0 = rt * kBM;  // first row of the tile inside the unit
-  const int64_t rows = (p.M_rows - r0) < kBM ? (p.M_rows - r0) : kBM;
-  // query positions l = r % L of the tile's rows: the smallest and the largest
-  const bool wraps = rows >= p.L || (r0 % p.L) + rows > p.L;
-  const int64_t l_first = wraps ? 0 : r0 % p.L;
-  const int64_t l_last = wraps ? p.L - 1 : (r0 + rows - 1) % p.L;
-  int64_t need = ctx_limit;
-  if (p.causal) {
-    const int64_t lim = l_last + ctx - p.L + 1;
-    if (lim < need) need = lim;
-  }
-  if (ctx <= 0 || need < 0) need = 0;
-  const int64_t n_tiles_unit = (need + kBN - 1) / kBN;
-  const int64_t n_chunks_unit = n_tiles_unit > 0 ? (n_tiles_unit + p.ct - 1) / p.ct : 1;
-  if (c >= n_chunks_unit) return;  // nothing of this unit left for this chunk (whole CTA, before any set-up)
-  const int64_t t_begin = c * p.ct;  // first 64-key tile of the chunk
-  const int n_tiles = (int)(n_tiles_unit - t_begin < p.ct ? n_tiles_unit - t_begin : p.ct);
-
-  // ---------------------------------------------------------------- producer (warp 4)
-  // The whole warp runs the loop (warp-uniform values stay on the uniform datapath) and
-  // one elected lane issues the copies.  Loads run in the order the MMA warp consumes
-  // them: K_0, K_1, V_0, K_2, V_1, ...  The first kKStages iterations need no free stage:
-  // the producer initialises the mbarriers itself and issues them before the block
-  // barrier, so TMEM allocation and the other warps' set-up overlap the first copies.
-  bool prod_leader = false;
-  const int kvh_i = (int)kvh, b_i = (int)b;
-  const int32_t* bt_row = p.dense ? nullptr : p.block_table + b * p.mp;
-  constexpr int kPagesPerTile = kBN / 16;  // paged path: page_size == 16
-  int ids_k[kPagesPerTile], ids_v[kPagesPerTile];  // page ids of tile t (K) and t-1 (V)
-  int k_issued = 0, v_issued = 0, t_next = 0;
-  // issue the copies of one 64-token K or V tile into `dst`, completing on `full`
-  auto issue = [&](const CUtensorMap* tm, uint8_t* dst, uint64_t* full, int j, const int* pid) {
-    if (prod_leader) {
-      mbar_arrive_expect_tx(full, kTileBytes);
-      if (p.dense) {
-        const int key0 = (int)((t_begin + j) * kBN);
-        tma_load_4d(dst, tm, 0, key0, kvh_i, b_i, full);
-        tma_load_4d(dst + kBN * 128, tm, 64, key0, kvh_i, b_i, full);
-      } else {
-#pragma unroll
-        for (int g = 0; g < kPagesPerTile; ++g) {
-          tma_load_4d(dst + g * 16 * 128, tm, 0, 0, kvh_i, pid[g], full);
-          tma_load_4d(dst + kBN * 128 + g * 16 * 128, tm, 64, 0, kvh_i, pid[g], full);
-        }
-      }
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
+    for (int s = 0; s < kKStages; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
     }
-    __syncwarp();
-  };
-  // loop iteration t: K_t (t < n_tiles) and V_{t-1} (t >= 1); false if a wait expired
-  // Paged calls: the page ids of 8 tiles (32 pages) sit one per lane of the producer
-  // warp and are loaded one 8-tile block ahead, so no block-table read stands in front
-  // of a copy.  Lane i of block blk holds page blk*32 + i of the chunk; holes and pages
-  // past the table read as the out-of-range page P (TMA fills zeros).
-  int id_cur = 0, id_next = 0, id_blk = 0;
-  auto load_ids = [&](int blk) -> int {
-    const int pidx = (int)(t_begin * kPagesPerTile) + blk * 32 + lane;
-    const int id = pidx < (int)p.mp ? bt_row[pidx] : -1;
-    return (id < 0 || id >= (int)p.P) ? (int)p.P : id;
-  };
-  // page g of chunk tile t (t in the current or the next 8-tile block); all 32 lanes call it
-  auto page_id = [&](int t, int g) -> int {
-    const int v_cur = __shfl_sync(0xffffffffu, id_cur, (t % 8) * kPagesPerTile + g);
-    const int v_next = __shfl_sync(0xffffffffu, id_next, (t % 8) * kPagesPerTile + g);
-    return t / 8 == id_blk ? v_cur : v_next;
-  };
-  auto produce = [&](int t) -> bool {
-    if (t < n_tiles) {
-      const int s = t % kKStages;
-      if (t >= kKStages && !warp_wait(&k_empty[s], ((t / kKStages) & 1) ^ 1)) return false;
-      if (!p.dense) {
-        if (t / 8 != id_blk) {  // entering the next block: shift, and load the one after
-          id_cur = id_next;
-          id_blk = t / 8;
-          id_next = load_ids(id_blk + 1);
-        }
-#pragma unroll
-        for (int g = 0; g < kPagesPerTile; ++g) ids_k[g] = page_id(t, g);
-      }
-      issue(&tm_k, sK + s * kTileBytes, &k_full[s], t, ids_k);
-      k_issued = t + 1;
-      // Grouped (decode-like) calls stream K/V from HBM once: the rings are only a few
-      // tiles deep, so tile t + kPrefetchTiles is pulled into L2 now.
-      const int tp = t + kPrefetchTiles;
-      if (p.grouped && p.prefetch && tp < n_tiles) {
-        if (prod_leader) {
-          if (p.dense) {
-            const int key0 = (int)((t_begin + tp) * kBN);
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              tma_prefetch_4d(&tm_k, h * 64, key0, kvh_i, b_i);
-              tma_prefetch_4d(&tm_v, h * 64, key0, kvh_i, b_i);
-            }
-          }
-        }
-        if (!p.dense) {
-          int pf[kPagesPerTile];
-#pragma unroll
-          for (int g = 0; g < kPagesPerTile; ++g) pf[g] = page_id(tp, g);
-          if (prod_leader) {
-#pragma unroll
-            for (int g = 0; g < kPagesPerTile; ++g) {
-              if (pf[g] < (int)p.P) {
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                  tma_prefetch_4d(&tm_k, h * 64, 0, kvh_i, pf[g]);
-                  tma_prefetch_4d(&tm_v, h * 64, 0, kvh_i, pf[g]);
-                }
-              }
-            }
-          }
-        }
-        __syncwarp();
-      }
+    for (int s = 0; s < kVStages; ++s) {
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
     }
-    if (t >= 1) {
-      const int j = t - 1, s = j % kVStages;
-      if (j >= kVStages && !warp_wait(&v_empty[s], ((j / kVStages) & 1) ^ 1)) return false;
-      issue(&tm_v, sV + s * kTileBytes, &v_full[s], j, ids_v);
-      v_issued = j + 1;
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 128);
     }
-#pragma unroll
-    for (int g = 0; g < kPagesPerTile; ++g) ids_v[g] = ids_k[g];
-    return true;
-  };
-  static_assert(kVStages + 1 >= kKStages, "iterations t < kKStages must not wait for a V stage");
-
-  if (warp == 4) {
-    prod_leader = elect_one();
-    if (prod_leader) {
-      mbar_init(q_full, 1);
-      for (int s = 0; s < kKStages; ++s) {
-        mbar_init(&k_full[s], 1);
-        mbar_init(&k_empty[s], 1);
-      }
-      for (int s = 0; s < kVStages; ++s) {
-        mbar_init(&v_full[s], 1);
-        mbar_init(&v_empty[s], 1);
-      }
-      for (int i = 0; i < 2; ++i) {
-        mbar_init(&s_full[i], 1);
-        mbar_init(&p_full[i], 128);
-      }
-      mbar_init(o_done, 1);
-      mbar_init(mma_done, 1);
-      *abort_flag = 0;
-      fence_mbar_init();
-      if (n_tiles > 0) {
-        prefetch_tmap(&tm_q);
-        prefetch_tmap(&tm_k);
-        prefetch_tmap(&tm_v);
-        mbar_arrive_expect_tx(q_full, kQBytes);
-        tma_load_3d(sQ, &tm_q, 0, (int)r0, (int)n, q_full);
-        tma_load_3d(sQ + kBM * 128, &tm_q, 64, (int)r0, (int)n, q_full);
-      }
+    mbar_init(o_done, 1);
+    mbar_init(item_done, 1);
+    mbar_init(o_free, 128);
+    mbar_init(mma_done, 1);
+    for (int i = 0; i < 4; ++i) {
+      mbar_init(&item_full[i], 1);
+      mbar_init(&item_empty[i], 5);
     }
-    __syncwarp();
-    if (!p.dense && n_tiles > 0) {
-      id_cur = load_ids(0);
-      id_next = load_ids(1);
-      // hole bitmask of the chunk's pages (read once, coalesced, before the block barrier)
-      const int n_pages = n_tiles * kPagesPerTile;
-      if (n_pages <= kHoleWords * 32) {
-        uint32_t any = 0;
-        for (int w0 = 0; w0 < n_pages; w0 += 32 * 4) {
-          bool hole[4];
-#pragma unroll
-          for (int x = 0; x < 4; ++x) {
-            const int i = w0 + x * 32 + lane;  // page of the chunk
-            const int pidx = (int)(t_begin * kPagesPerTile) + i;
-            const int id = (i < n_pages && pidx < (int)p.mp) ? bt_row[pidx] : 0;
-            hole[x] = i < n_pages && (pidx >= (int)p.mp || id < 0 || id >= (int)p.P);
-          }
-#pragma unroll
-          for (int x = 0; x < 4; ++x) {
-            const uint32_t bits = __ballot_sync(0xffffffffu, hole[x]);
-            any |= bits;
-            if (lane == 0 && w0 / 32 + x < kHoleWords) hole_bits[w0 / 32 + x] = bits;
-          }
-        }
-        if (lane == 0) *hole_state = any ? 1 : 0;
-      } else if (lane == 0) {
-        *hole_state = 2;
-      }
-    }
-    for (; t_next < kKStages && t_next <= n_tiles && n_tiles > 0; ++t_next) produce(t_next);  // no waits
+    *abort_flag = 0;
+    fence_mbar_init();
   }
   if (warp == 5) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
@@ -498,95 +377,252 @@ __global__ void __launch_bounds__(kThreads, 2)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t tO = tmem + 2 * kBN;
-  int64_t min_keys = p.causal ? (l_first + ctx - p.L + 1) : ctx_limit;  // fewest keys any row of the unit sees
-  const bool split = kSplit && min_keys < p.split_below;
+  constexpr int kPagesPerTile = kBN / 16;  // paged path: page_size == 16
+
+  // consumers of the item ring: slot k & 3 of the k-th published item
+  auto read_item = [&](int k, bool arrive) -> int64_t {
+    if (!warp_wait(&item_full[k & 3], (k >> 2) & 1)) return -2;
+    const int64_t v = *(volatile int64_t*)&item_ring[k & 3];
+    __syncwarp();
+    if (arrive && lane == 0) mbar_arrive(&item_empty[k & 3]);
+    return v;
+  };
+  // the unit's fewest keys seen by a row: bf16 P is split into hi + lo below split_below
+  auto split_of = [&](const Item& it) -> bool {
+    const int64_t min_keys = p.causal ? (it.l_first + it.ctx - p.L + 1) : it.ctx_limit;
+    return kSplit && min_keys < p.split_below;
+  };
 
   if (warp == 4) {
-    if (n_tiles > 0) {
-      bool ok = true;
-      for (; t_next <= n_tiles; ++t_next) {
-        if (!produce(t_next)) {
-          ok = false;
-          break;
-        }
-        if (__any_sync(0xffffffffu, *(volatile int*)abort_flag != 0)) break;
+    // ---------------------------------------------------------------- producer
+    // The whole warp runs the loop and one elected lane issues the copies.  Per item:
+    // publish the item index, load Q (once the previous item's last S has read sQ), then
+    // K_0, K_1, V_0, K_2, V_1, ... into the rings.
+    const bool leader = elect_one();
+    const int leader_lane = __ffs(__ballot_sync(0xffffffffu, leader)) - 1;
+    int gk = 0, gv = 0;  // K / V tiles issued by this CTA so far
+    int kq = 0, iw = 0;      // items published, items with keys
+    bool ok = true;
+    while (ok) {
+      const int slot = kq & 3;
+      if (kq >= 4 && !warp_wait(&item_empty[slot], ((kq >> 2) & 1) ^ 1)) {
+        ok = false;
+        break;
       }
-      if (prod_leader) {
-        if (!ok) {
-          record_error(p.err, kDevErrEmptyWait);
-          *(volatile int*)abort_flag = 1;
-        }
-        // drain: every issued load lands before the CTA may exit
-        if (!mbar_wait(q_full, 0)) record_error(p.err, kDevErrDrainWait);
-        auto drain = [&](uint64_t* full, int ns, int issued) {
-          for (int s = 0; s < ns && s < issued; ++s) {
-            const int last = s + ((issued - 1 - s) / ns) * ns;
-            if (!mbar_wait(&full[s], (last / ns) & 1)) record_error(p.err, kDevErrDrainWait);
-          }
-        };
-        drain(k_full, kKStages, k_issued);
-        drain(v_full, kVStages, v_issued);
+      int64_t item;
+      if (p.work_counter != nullptr) {
+        int v = 0;
+        if (leader) v = atomicAdd(p.work_counter, 1);
+        item = __shfl_sync(0xffffffffu, v, leader_lane);
+      } else {
+        item = (int64_t)blockIdx.x + (int64_t)kq * gridDim.x;
+      }
+      if (item >= p.n_items) item = -1;
+      if (leader) {
+        *(volatile int64_t*)&item_ring[slot] = item;
+        mbar_arrive(&item_full[slot]);
       }
       __syncwarp();
+      ++kq;
+      if (item < 0) break;
+      const Item it = decode_item(p, item);
+      if (it.n_tiles == 0) continue;
+      const int kvh_i = (int)it.kvh, b_i = (int)it.b;
+      const int32_t* bt_row = p.dense ? nullptr : p.block_table + it.b * p.mp;
+      if (iw > 0 && !warp_wait(q_empty, (iw - 1) & 1)) {
+        ok = false;
+        break;
+      }
+      if (leader) {
+        mbar_arrive_expect_tx(q_full, kQBytes);
+        tma_load_3d(sQ, &tm_q, 0, (int)it.r0, (int)it.n, q_full);
+        tma_load_3d(sQ + kBM * 128, &tm_q, 64, (int)it.r0, (int)it.n, q_full);
+      }
+      __syncwarp();
+      ++iw;
+      // Paged: the page ids of 8 tiles (32 pages) sit one per lane and are loaded one
+      // block ahead; holes and pages past the table read as page P (TMA fills zeros).
+      auto load_ids = [&](int blk) -> int {
+        const int pidx = (int)(it.t_begin * kPagesPerTile) + blk * 32 + lane;
+        const int id = pidx < (int)p.mp ? bt_row[pidx] : -1;
+        return (id < 0 || id >= (int)p.P) ? (int)p.P : id;
+      };
+      int id_cur = 0, id_next = 0, id_blk = 0;
+      if (!p.dense) {
+        id_cur = load_ids(0);
+        id_next = load_ids(1);
+      }
+      auto page_id = [&](int t, int g) -> int {
+        const int v_cur = __shfl_sync(0xffffffffu, id_cur, (t % 8) * kPagesPerTile + g);
+        const int v_next = __shfl_sync(0xffffffffu, id_next, (t % 8) * kPagesPerTile + g);
+        return t / 8 == id_blk ? v_cur : v_next;
+      };
+      int ids_k[kPagesPerTile], ids_v[kPagesPerTile];
+      auto issue = [&](const CUtensorMap* tm, uint8_t* dst, uint64_t* full, int t, const int* pid) {
+        if (leader) {
+          mbar_arrive_expect_tx(full, kTileBytes);
+          if (p.dense) {
+            const int key0 = (int)((it.t_begin + t) * kBN);
+            tma_load_4d(dst, tm, 0, key0, kvh_i, b_i, full);
+            tma_load_4d(dst + kBN * 128, tm, 64, key0, kvh_i, b_i, full);
+          } else {
+#pragma unroll
+            for (int g = 0; g < kPagesPerTile; ++g) {
+              tma_load_4d(dst + g * 16 * 128, tm, 0, 0, kvh_i, pid[g], full);
+              tma_load_4d(dst + kBN * 128 + g * 16 * 128, tm, 64, 0, kvh_i, pid[g], full);
+            }
+          }
+        }
+        __syncwarp();
+      };
+      for (int t = 0; ok && t <= it.n_tiles; ++t) {
+        if (t < it.n_tiles) {  // K_t
+          const int s = gk % kKStages;
+          if (gk >= kKStages && !warp_wait(&k_empty[s], (uint32_t)(((gk / kKStages) & 1) ^ 1))) {
+            ok = false;
+            break;
+          }
+          if (!p.dense) {
+            if (t / 8 != id_blk) {
+              id_cur = id_next;
+              id_blk = t / 8;
+              id_next = load_ids(id_blk + 1);
+            }
+#pragma unroll
+            for (int g = 0; g < kPagesPerTile; ++g) ids_k[g] = page_id(t, g);
+          }
+          issue(&tm_k, sK + s * kTileBytes, &k_full[s], t, ids_k);
+          ++gk;
+        }
+        if (t >= 1) {  // V_{t-1}
+          const int s = gv % kVStages;
+          if (gv >= kVStages && !warp_wait(&v_empty[s], (uint32_t)(((gv / kVStages) & 1) ^ 1))) {
+            ok = false;
+            break;
+          }
+          issue(&tm_v, sV + s * kTileBytes, &v_full[s], t - 1, ids_v);
+          ++gv;
+        }
+#pragma unroll
+        for (int g = 0; g < kPagesPerTile; ++g) ids_v[g] = ids_k[g];
+        if (__any_sync(0xffffffffu, *(volatile int*)abort_flag != 0)) ok = false;
+      }
     }
+    if (leader) {
+      if (!ok) {
+        record_error(p.err, kDevErrEmptyWait);
+        *(volatile int*)abort_flag = 1;
+        // consumers waiting for an item index are released with the end marker
+        for (int k = kq; k < kq + 4; ++k) {
+          *(volatile int64_t*)&item_ring[k & 3] = -1;
+          mbar_arrive(&item_full[k & 3]);
+        }
+      }
+      // drain: every issued load lands before the CTA may exit
+      if (iw > 0 && !mbar_wait(q_full, (iw - 1) & 1)) record_error(p.err, kDevErrDrainWait);
+      auto drain = [&](uint64_t* full, int ns, int issued) {
+        for (int s = 0; s < ns && s < issued; ++s) {
+          const int last = s + ((issued - 1 - s) / ns) * ns;
+          if (!mbar_wait(&full[s], (uint32_t)((last / ns) & 1))) record_error(p.err, kDevErrDrainWait);
+        }
+      };
+      drain(k_full, kKStages, gk);
+      drain(v_full, kVStages, gv);
+    }
+    __syncwarp();
   } else if (warp == 5) {
     // ---------------------------------------------------------------- MMA issuer
     // The whole warp waits and loops; one elected lane issues the MMAs and the commits
     // (a commit tracks the MMAs of the thread that issues it, so it is always the same lane).
-    if (n_tiles > 0) {
-      const bool leader = elect_one();
-      const uint32_t id_qk = idesc<T>(false, kBN);
-      const uint32_t id_pv = idesc<T>(true, kD);
-      // Descriptors of the first 16-column slice of Q, K stage 0 and V stage 0; a byte
-      // offset o inside shared memory adds o >> 4 to the start-address field.
-      // One thread can issue a tcgen05.mma only every ~47 cycles, and descriptor
-      // arithmetic between two MMAs adds ~26 more: the Q descriptors are computed once,
-      // a tile's K or V descriptors in one batch before its MMAs.
-      uint64_t dq[8];
-      {
-        const uint64_t q0 = smem_desc(smem_u32(sQ), 16, 1024);
+    const bool leader = elect_one();
+    const uint32_t id_qk = idesc<T>(false, kBN);
+    const uint32_t id_pv = idesc<T>(true, kD);
+    // One thread can issue a tcgen05.mma only every ~47 cycles, and descriptor
+    // arithmetic between two MMAs adds ~26 more: the Q descriptors are computed once,
+    // a tile's K or V descriptors in one batch before its MMAs.
+    uint64_t dq[8];
+    {
+      const uint64_t q0 = smem_desc(smem_u32(sQ), 16, 1024);
 #pragma unroll
-        for (int ks = 0; ks < 8; ++ks) dq[ks] = q0 + (uint64_t)((((ks >> 2) * (kBM * 128)) + (ks & 3) * 32) >> 4);
+      for (int ks = 0; ks < 8; ++ks) dq[ks] = q0 + (uint64_t)((((ks >> 2) * (kBM * 128)) + (ks & 3) * 32) >> 4);
+    }
+    const uint64_t dk = smem_desc(smem_u32(sK), 16, 1024);
+    const uint64_t dv = smem_desc(smem_u32(sV), kBN * 128, 1024);
+    int gs = 0, gp = 0;  // S / PV tiles issued by this CTA so far
+    int kq = 0, iw = 0;
+    bool ok = true;
+    // K of the next S landed (checked before the wait on the PV it overwrites, which it
+    // does not depend on)
+    auto wait_k = [&]() -> bool { return warp_wait(&k_full[gs % kKStages], (uint32_t)((gs / kKStages) & 1)); };
+    // S_G = Q K^T into TMEM buffer G&1 from K stage G % kKStages (after wait_k)
+    auto issue_s = [&](bool last_of_item) {
+      const int s = gs % kKStages;
+      tc_fence_after();
+      const uint64_t dks = dk + (uint64_t)((s * kTileBytes) >> 4);
+      uint64_t db[8];
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) db[ks] = dks + (uint64_t)((((ks >> 2) * (kBN * 128)) + (ks & 3) * 32) >> 4);
+      const uint32_t td = tmem + (uint32_t)((gs & 1) * kBN);
+      if (leader) {
+#pragma unroll
+        for (int ks = 0; ks < kD / 16; ++ks) mma_f16(td, dq[ks], db[ks], id_qk, ks > 0 ? 1u : 0u);
+        mma_commit(&s_full[gs & 1]);
+        mma_commit(&k_empty[s]);
+        if (last_of_item) mma_commit(q_empty);
       }
-      const uint64_t dk = smem_desc(smem_u32(sK), 16, 1024);
-      const uint64_t dv = smem_desc(smem_u32(sV), kBN * 128, 1024);
-      bool ok = warp_wait(q_full, 0);
-      // K_j landed (checked before the wait on PV_{j-2}, which it does not depend on)
-      auto wait_k = [&](int j) -> bool { return warp_wait(&k_full[j % kKStages], (j / kKStages) & 1); };
-      auto issue_s = [&](int j) -> bool {
-        const int s = j % kKStages;
-        tc_fence_after();
-        // 16-column K slice ks: 64-column half ks/4 (kBN rows of 128 B), 32 B per slice
-        const uint64_t dks = dk + (uint64_t)((s * kTileBytes) >> 4);
-        uint64_t db[8];
-#pragma unroll
-        for (int ks = 0; ks < 8; ++ks) db[ks] = dks + (uint64_t)((((ks >> 2) * (kBN * 128)) + (ks & 3) * 32) >> 4);
-        const uint32_t td = tmem + (uint32_t)((j & 1) * kBN);
-        if (leader) {
-#pragma unroll
-          for (int ks = 0; ks < kD / 16; ++ks) mma_f16(td, dq[ks], db[ks], id_qk, ks > 0 ? 1u : 0u);
-          mma_commit(&s_full[j & 1]);
-          mma_commit(&k_empty[s]);
+      __syncwarp();
+      ++gs;
+    };
+    while (ok) {
+      const int64_t item = read_item(kq, true);
+      ++kq;
+      if (item < 0) {
+        ok = item == -1;
+        break;
+      }
+      const Item it = decode_item(p, item);
+      const int n = it.n_tiles;
+      if (n == 0) continue;
+      const bool split = split_of(it);
+      // S buffers: every PV of the previous item done; Q of this item landed
+      if (iw > 0 && !warp_wait(item_done, (iw - 1) & 1)) {
+        ok = false;
+        break;
+      }
+      if (!warp_wait(q_full, iw & 1)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      if (!wait_k()) {
+        ok = false;
+        break;
+      }
+      issue_s(n == 1);
+      if (n > 1) {
+        if (!wait_k()) {
+          ok = false;
+          break;
         }
-        __syncwarp();
-        return true;
-      };
-      if (ok) ok = wait_k(0) && issue_s(0);
-      if (ok && n_tiles > 1) ok = wait_k(1) && issue_s(1);
-      for (int j = 0; ok && j < n_tiles; ++j) {
-        // P_j (over S_j's TMEM columns) written by the softmax warps, V_j landed
-        const int s = j % kVStages;
-        if (!warp_wait(&p_full[j & 1], (j >> 1) & 1) || !warp_wait(&v_full[s], (j / kVStages) & 1)) {
+        issue_s(n == 2);
+      }
+      for (int j = 0; j < n; ++j) {
+        // P_j written by the softmax warps, V_j landed; the first PV of an item overwrites
+        // O, which the softmax warps must have read out for the previous item
+        const int vs = gp % kVStages;
+        if (!warp_wait(&p_full[gp & 1], (uint32_t)((gp >> 1) & 1)) ||
+            !warp_wait(&v_full[vs], (uint32_t)((gp / kVStages) & 1)) ||
+            (j == 0 && iw > 0 && !warp_wait(o_free, (iw - 1) & 1))) {
           ok = false;
           break;
         }
         tc_fence_after();
         // V is MN-major: 64-column halves kBN*128 bytes apart (LBO), 8-token groups 1024 apart (SBO)
-        const uint64_t dvs = dv + (uint64_t)((s * kTileBytes) >> 4);
+        const uint64_t dvs = dv + (uint64_t)((vs * kTileBytes) >> 4);
         uint64_t db[4];
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks) db[ks] = dvs + (uint64_t)((ks * 16 * 128) >> 4);
-        const uint32_t tp = tmem + (uint32_t)((j & 1) * kBN);
+        const uint32_t tp = tmem + (uint32_t)((gp & 1) * kBN);
         if (leader) {
 #pragma unroll
           for (int ks = 0; ks < kBN / 16; ++ks) {
@@ -594,194 +630,48 @@ __global__ void __launch_bounds__(kThreads, 2)
             if (split) mma_f16_ts(tO, tp + (uint32_t)(kBN / 2 + ks * 8), db[ks], id_pv, 1u);
           }
           mma_commit(o_done);
-          mma_commit(&v_empty[s]);
+          mma_commit(&v_empty[vs]);
+          if (j == n - 1) mma_commit(item_done);
         }
         __syncwarp();
+        const int gj = gp++;
         // S_{j+2} reuses S_j's TMEM columns, which hold P_j: wait until PV_j has
-        // finished reading them (o_done phase j) before overwriting.
-        if (j + 2 < n_tiles) {
-          if (!wait_k(j + 2) || !warp_wait(o_done, j & 1)) {
+        // finished reading them (o_done phase of PV_j) before overwriting.
+        if (j + 2 < n) {
+          if (!wait_k() || !warp_wait(o_done, (uint32_t)(gj & 1))) {
             ok = false;
             break;
           }
-          ok = issue_s(j + 2);
+          issue_s(j + 2 == n - 1);
         }
       }
-      if (leader) {
-        if (!ok) {
-          record_error(p.err, kDevErrMmaWait);
-          *(volatile int*)abort_flag = 1;
-        }
-        mma_commit(mma_done);
-      }
-      __syncwarp();
+      ++iw;
     }
+    if (leader) {
+      if (!ok) {
+        record_error(p.err, kDevErrMmaWait);
+        *(volatile int*)abort_flag = 1;
+      }
+      mma_commit(mma_done);
+    }
+    __syncwarp();
   } else {
     // ---------------------------------------------------------------- softmax warps 0-3
     const int row = warp * 32 + lane;            // TMEM lane == query row in the tile
     const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-    const int64_t lpos = (r0 + row) % p.L;       // the row's position among the L query tokens
-    // last key this row may see: inside the context and, when causal, key <= l + ctx - L
-    int64_t last_key = ctx_limit - 1;
-    if (p.causal && lpos + ctx - p.L < last_key) last_key = lpos + ctx - p.L;
-    if (row >= rows) last_key = -1;
-    const float sl2 = p.scale_log2;  // > 0, so max(s) * sl2 == max(s * sl2)
-    float m = -INFINITY, lsum = 0.f;  // running max (log2 units, lazily updated) and sum
+    const float sl2 = p.scale_log2;              // > 0, so max(s) * sl2 == max(s * sl2)
+    const int esz = p.out_dtype == NVM_F32 ? 4 : 2;
+    int gt = 0;  // tiles processed by this CTA so far
+    int kq = 0, iw = 0;
     bool ok = true;
-    for (int j = 0; j < n_tiles; ++j) {
-      if (!warp_wait(&s_full[j & 1], (j >> 1) & 1)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const uint32_t tS = tmem + lane_base + (uint32_t)((j & 1) * kBN);
-      float sv[kBN];
-#pragma unroll
-      for (int c = 0; c < kBN / 32; ++c) tmem_ld32(tS + c * 32, *reinterpret_cast<float(*)[32]>(&sv[c * 32]));
-      tmem_wait_ld();
-      const int64_t key0 = (t_begin + j) * kBN;
-      // Only tiles that cross some row's last visible key (the causal diagonal, the
-      // context end, rows past L) pay for the mask: one compare per score.
-      const int64_t vis64 = last_key - key0;  // in-tile index of the row's last visible key
-      if (__any_sync(0xffffffffu, vis64 < kBN - 1)) {
-        const int vis = vis64 < -1 ? -1 : (int)vis64;
-#pragma unroll
-        for (int c = 0; c < kBN; ++c) sv[c] = c <= vis ? sv[c] : -INFINITY;
-      }
-      const int hstate = p.dense ? 0 : *hole_state;
-      if (hstate == 1) {  // holes: the 16-token groups of missing pages are masked
-        const uint32_t bits = (hole_bits[(j * kPagesPerTile) / 32] >> ((j * kPagesPerTile) % 32)) & 0xFu;
-        if (bits != 0) {
-#pragma unroll
-          for (int g = 0; g < kPagesPerTile; ++g) {
-            if ((bits >> g) & 1u) {
-#pragma unroll
-              for (int c = 0; c < 16; ++c) sv[g * 16 + c] = -INFINITY;
-            }
-          }
-        }
-      } else if (hstate == 2) {
-#pragma unroll
-        for (int g = 0; g < kBN / 16; ++g) {
-          const int64_t pidx = (key0 + g * 16) / p.ps;
-          const int64_t id = pidx < p.mp ? (int64_t)p.block_table[b * p.mp + pidx] : -1;
-          if (id < 0 || id >= p.P) {
-#pragma unroll
-            for (int c = 0; c < 16; ++c) sv[g * 16 + c] = -INFINITY;
-          }
-        }
-      }
-      // row max as a tree (8 independent chains), not one 64-long dependency chain
-      float mv[8];
-#pragma unroll
-      for (int x = 0; x < 8; ++x) mv[x] = sv[x];
-#pragma unroll
-      for (int c = 8; c < kBN; c += 8) {
-#pragma unroll
-        for (int x = 0; x < 8; ++x) mv[x] = fmaxf(mv[x], sv[c + x]);
-      }
-      const float mx = fmaxf(fmaxf(fmaxf(mv[0], mv[1]), fmaxf(mv[2], mv[3])), fmaxf(fmaxf(mv[4], mv[5]), fmaxf(mv[6], mv[7])));
-      const float mx_s = mx * sl2;
-      // lazy max: keep the old reference max unless the new one exceeds it by > 8
-      float m_ref = m;
-      bool rescale = false;
-      if (mx_s > -INFINITY && (m == -INFINITY || mx_s > m + kRescaleThreshold)) {
-        rescale = m != -INFINITY;
-        m_ref = mx_s;
-      }
-      const float mu = m_ref == -INFINITY ? 0.f : m_ref;
-      const float alpha = ex2_ftz(m - mu);  // 0 when m == -inf
-      // p = 2^(s * sl2 - mu) on packed pairs.  Most exponentials run on the MUFU unit;
-      // outside split tiles the pairs selected by kEmuPairs run on the FMA pipe instead
-      // (exp2_fma2), which keeps MUFU from setting the tile rate.
-      const float2 sl2v = make_float2(sl2, sl2), nmu = make_float2(-mu, -mu);
-      float2 acc[4];
-#pragma unroll
-      for (int x = 0; x < 4; ++x) acc[x] = make_float2(0.f, 0.f);
-      if (split) {
-#pragma unroll
-        for (int q = 0; q < kBN / 2; ++q) {
-          const float2 x2 = __ffma2_rn(make_float2(sv[2 * q], sv[2 * q + 1]), sl2v, nmu);
-          const float2 e = make_float2(ex2_ftz(x2.x), ex2_ftz(x2.y));
-          sv[2 * q] = e.x;
-          sv[2 * q + 1] = e.y;
-          acc[q & 3] = __fadd2_rn(acc[q & 3], e);
-        }
-      } else {
-#pragma unroll
-        for (int q = 0; q < kBN / 2; ++q) {
-          const float2 x2 = __ffma2_rn(make_float2(sv[2 * q], sv[2 * q + 1]), sl2v, nmu);
-          const float2 e = ((kEmuPairs >> q) & 1u) ? exp2_fma2<T>(x2) : make_float2(ex2_ftz(x2.x), ex2_ftz(x2.y));
-          sv[2 * q] = e.x;
-          sv[2 * q + 1] = e.y;
-          acc[q & 3] = __fadd2_rn(acc[q & 3], e);
-        }
-      }
-      const float2 a01 = __fadd2_rn(__fadd2_rn(acc[0], acc[1]), __fadd2_rn(acc[2], acc[3]));
-      // A row with no visible key yet keeps a zero sum (so it ends as zeros): exp2_fma2
-      // turns its -inf scores into 2^-125, not 0.  Next to a visible key's p >= 2^-8,
-      // 2^-125 is nothing.
-      const float rs = m_ref == -INFINITY ? 0.f : a01.x + a01.y;
-      lsum = (m == -INFINITY ? 0.f : lsum * alpha) + rs;
-      m = m_ref;
-      if (__any_sync(0xffffffffu, rescale)) {
-        // O must hold PV_{j-1} before it is rescaled
-        if (!warp_wait(o_done, (j - 1) & 1)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const float f = rescale ? alpha : 1.f;
-#pragma unroll 1
-        for (int c = 0; c < kD / 32; ++c) {
-          float ov[32];
-          tmem_ld32(tO + lane_base + c * 32, ov);
-          tmem_wait_ld();
-#pragma unroll
-          for (int x = 0; x < 32; ++x) ov[x] *= f;
-          tmem_st32(tO + lane_base + c * 32, ov);
-        }
-      }
-      // P over S_j's columns: packed pairs, hi in columns [0, kBN/2), lo (bf16 split) after
-      {
-        uint32_t hi[32];
-#pragma unroll
-        for (int x = 0; x < 32; ++x) hi[x] = cvt_pack<T>(sv[2 * x], sv[2 * x + 1]);
-        tmem_st32u(tS, hi);
-        if (split) {
-          uint32_t lo[32];
-#pragma unroll
-          for (int x = 0; x < 32; ++x) {
-            // bf16 -> f32 is exact: the bf16 bits become the high half of the f32
-            const float h0 = __uint_as_float(hi[x] << 16), h1 = __uint_as_float(hi[x] & 0xFFFF0000u);
-            lo[x] = cvt_pack<T>(sv[2 * x] - h0, sv[2 * x + 1] - h1);
-          }
-          tmem_st32u(tS + kBN / 2, lo);
-        }
-      }
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(&p_full[j & 1]);
-    }
-    // final O: wait for the last PV, normalise, stage through shared memory, store coalesced.
-    // The wait is on mma_done (one completion per CTA), not on o_done: a parity wait
-    // only tells "phase k done" from "phase k+1 done", and these warps may arrive here
-    // while PV_{n-2} is still running, when o_done's parity already matches PV_{n-1}'s.
-    if (ok && n_tiles > 0 && !warp_wait(mma_done, 0)) ok = false;
-    if (!ok) {
-      record_error(p.err, kDevErrFullWait);
-      *(volatile int*)abort_flag = 1;
-    }
-    tc_fence_after();
-    // O rows -> shared memory in the TMA store's 128B-swizzled box layout: the tile is
-    // split into boxes of 128 bytes of columns (32 fp32 or 64 16-bit values) x 128 rows,
-    // 16 KB each; row r's 16-byte chunk c of a box sits at r * 128 + ((c ^ (r & 7)) << 4).
-    // The K/V ring is free once every MMA is done.
-    const bool f32_out = p.out_dtype == NVM_F32;
+    // With one item per CTA (stage_out) the K/V ring is free once the item's MMAs are done:
+    // O rows go to shared memory in the TMA store's 128B-swizzled box layout (boxes of 128
+    // bytes of columns x 128 rows, 16 KB each; row r's 16-byte chunk c of a box at
+    // r * 128 + ((c ^ (r & 7)) << 4)) and leave with bulk tensor stores.  Otherwise the
+    // next item's tiles are already streaming into the ring and each row is stored directly.
     uint8_t* srow = sK + row * 128;
-    // 32 values of this row (columns c0 .. c0+31), times inv, into the staging boxes
     auto stage32 = [&](const float* ov, int c0, float inv) {
-      if (f32_out) {
+      if (esz == 4) {
         uint8_t* box = srow + (c0 / 32) * (kBM * 128);
 #pragma unroll
         for (int x = 0; x < 8; ++x)
@@ -808,101 +698,313 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
       }
     };
-    bool store = true;
-    if (n_chunks_unit == 1) {
-      const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
-      // two 32-column TMEM loads in flight per wait
-#pragma unroll 1
-      for (int c1 = 0; c1 < kD; c1 += 64) {
-        float ov2[64];
-        if (n_tiles > 0) {
-          tmem_ld32(tO + lane_base + c1, *reinterpret_cast<float(*)[32]>(&ov2[0]));
-          tmem_ld32(tO + lane_base + c1 + 32, *reinterpret_cast<float(*)[32]>(&ov2[32]));
-          tmem_wait_ld();
-        } else {
-#pragma unroll
-          for (int x = 0; x < 64; ++x) ov2[x] = 0.f;
-        }
-        stage32(ov2, c1, inv);
-        stage32(ov2 + 32, c1 + 32, inv);
-      }
-    } else {
-      // Split-K: leave this chunk's (m, l) and unnormalised O rows in the workspace ...
-      const int64_t prow = (u * p.n_chunks + c) * p.rows_real + row;
-      if (row < rows) p.part_ml[prow] = make_float2(m, lsum);  // m = -inf: no visible key in this chunk
-#pragma unroll 1
-      for (int c1 = 0; c1 < kD; c1 += 64) {
-        float ov2[64];
-        tmem_ld32(tO + lane_base + c1, *reinterpret_cast<float(*)[32]>(&ov2[0]));
-        tmem_ld32(tO + lane_base + c1 + 32, *reinterpret_cast<float(*)[32]>(&ov2[32]));
-        tmem_wait_ld();
-        if (row < rows) {
-          float4* po = reinterpret_cast<float4*>(p.part_o + prow * kD + c1);
-#pragma unroll
-          for (int x = 0; x < 16; ++x) po[x] = make_float4(ov2[4 * x], ov2[4 * x + 1], ov2[4 * x + 2], ov2[4 * x + 3]);
-        }
-      }
-      // ... and the unit's last chunk to finish merges them (log-sum-exp weights).
-      __threadfence();
-      named_barrier(1, 128);
-      int* last_flag = reinterpret_cast<int*>(tmem_slot + 2);
-      if (row == 0) *(volatile int*)last_flag = atomicAdd(&p.counters[u], 1) == (int)n_chunks_unit - 1;
-      named_barrier(1, 128);
-      store = *(volatile int*)last_flag != 0;
-      if (store) {
-        __threadfence();
-        const int64_t base = u * p.n_chunks * p.rows_real + row;  // + cc * rows_real
-        float mx = -INFINITY, lt = 0.f;
-        if (row < rows) {
-          for (int64_t cc = 0; cc < n_chunks_unit; ++cc) mx = fmaxf(mx, __ldcg(&p.part_ml[base + cc * p.rows_real]).x);
-          for (int64_t cc = 0; cc < n_chunks_unit; ++cc) {
-            const float2 ml = __ldcg(&p.part_ml[base + cc * p.rows_real]);
-            if (ml.x != -INFINITY) lt += ml.y * exp2f(ml.x - mx);
-          }
-        }
-        const float inv = lt > 0.f ? 1.f / lt : 0.f;
-#pragma unroll 1
-        for (int c0 = 0; c0 < kD; c0 += 32) {
-          float acc[32];
-#pragma unroll
-          for (int x = 0; x < 32; ++x) acc[x] = 0.f;
-          if (row < rows) {
-            for (int64_t cc = 0; cc < n_chunks_unit; ++cc) {
-              const float2 ml = __ldcg(&p.part_ml[base + cc * p.rows_real]);
-              if (ml.x == -INFINITY) continue;
-              const float w = exp2f(ml.x - mx);
-              const float4* po = reinterpret_cast<const float4*>(p.part_o + (base + cc * p.rows_real) * kD + c0);
-#pragma unroll
-              for (int x = 0; x < 8; ++x) {
-                const float4 o4 = __ldcg(po + x);
-                acc[4 * x] += w * o4.x;
-                acc[4 * x + 1] += w * o4.y;
-                acc[4 * x + 2] += w * o4.z;
-                acc[4 * x + 3] += w * o4.w;
-              }
-            }
-          }
-          stage32(acc, c0, inv);
-        }
-        if (row == 0) p.counters[u] = 0;  // tickets start at zero for the next call
-      }
-    }
-    if (store) {
+    // the staged tile -> global memory (rows past the unit's end fall outside the tensor map)
+    auto flush_staged = [&](const Item& it) {
       fence_async_smem();  // generic-proxy stores -> visible to the TMA engine
       named_barrier(1, 128);
       if (row == 0) {
-        // Rows past the unit's end fall outside the tensor map and are not written.
-        const int cols_per_box = f32_out ? 32 : 64;
+        const int cols_per_box = esz == 4 ? 32 : 64;
         for (int bx = 0; bx < kD / cols_per_box; ++bx)
-          tma_store_3d(&tm_o, sK + bx * (kBM * 128), bx * cols_per_box, (int)r0, (int)n);
+          tma_store_3d(&tm_o, sK + bx * (kBM * 128), bx * cols_per_box, (int)it.r0, (int)it.n);
         bulk_commit();
         bulk_wait_read_all();
       }
+    };
+    // 32 values of this row (columns c0 .. c0+31), times inv, straight to global memory
+    auto store32 = [&](uint8_t* orow, const float* ov, int c0, float inv) {
+      if (esz == 4) {
+        float4* d = reinterpret_cast<float4*>(orow + c0 * 4);
+#pragma unroll
+        for (int x = 0; x < 8; ++x) d[x] = make_float4(ov[4 * x] * inv, ov[4 * x + 1] * inv, ov[4 * x + 2] * inv, ov[4 * x + 3] * inv);
+      } else {
+        uint4* d = reinterpret_cast<uint4*>(orow + c0 * 2);
+#pragma unroll
+        for (int x = 0; x < 4; ++x) {
+          if (p.out_dtype == NVM_BF16) {
+            d[x] = make_uint4(cvt_pack<__nv_bfloat16>(ov[8 * x] * inv, ov[8 * x + 1] * inv),
+                              cvt_pack<__nv_bfloat16>(ov[8 * x + 2] * inv, ov[8 * x + 3] * inv),
+                              cvt_pack<__nv_bfloat16>(ov[8 * x + 4] * inv, ov[8 * x + 5] * inv),
+                              cvt_pack<__nv_bfloat16>(ov[8 * x + 6] * inv, ov[8 * x + 7] * inv));
+          } else {
+            d[x] = make_uint4(cvt_pack<__half>(ov[8 * x] * inv, ov[8 * x + 1] * inv),
+                              cvt_pack<__half>(ov[8 * x + 2] * inv, ov[8 * x + 3] * inv),
+                              cvt_pack<__half>(ov[8 * x + 4] * inv, ov[8 * x + 5] * inv),
+                              cvt_pack<__half>(ov[8 * x + 6] * inv, ov[8 * x + 7] * inv));
+          }
+        }
+      }
+    };
+    while (ok) {
+      const int64_t item = read_item(kq, true);
+      ++kq;
+      if (item < 0) {
+        ok = item == -1;
+        break;
+      }
+      const Item it = decode_item(p, item);
+      if (!it.valid) continue;
+      const int n = it.n_tiles;
+      const bool row_ok = row < it.rows;
+      uint8_t* orow = reinterpret_cast<uint8_t*>(p.out) + ((it.n * p.M_rows) + it.r0 + row) * (int64_t)kD * esz;
+      if (n == 0) {  // no key: zero rows (a single chunk)
+        float z[32];
+#pragma unroll
+        for (int x = 0; x < 32; ++x) z[x] = 0.f;
+        if (row_ok)
+          for (int c0 = 0; c0 < kD; c0 += 32) store32(orow, z, c0, 0.f);
+        continue;
+      }
+      const bool split = split_of(it);
+      const int64_t lpos = (it.r0 + row) % p.L;  // the row's position among the L query tokens
+      // last key this row may see: inside the context and, when causal, key <= l + ctx - L
+      int64_t last_key = it.ctx_limit - 1;
+      if (p.causal && lpos + it.ctx - p.L < last_key) last_key = lpos + it.ctx - p.L;
+      if (!row_ok) last_key = -1;
+      // Paged: page ids two tiles ahead, lanes 0..3 hold page g = lane of a tile; the
+      // hole test happens when the tile is processed, so the load latency is hidden.
+      const int32_t* bt_row = p.dense ? nullptr : p.block_table + it.b * p.mp;
+      auto load_pid = [&](int t) -> int {
+        if (p.dense || lane >= kPagesPerTile || t >= n) return 0;
+        const int pidx = (int)(it.t_begin + t) * kPagesPerTile + lane;
+        return pidx < (int)p.mp ? bt_row[pidx] : -1;
+      };
+      int pid0 = load_pid(0), pid1 = load_pid(1);
+      float m = -INFINITY, lsum = 0.f;  // running max (log2 units, lazily updated) and sum
+      for (int j = 0; j < n; ++j) {
+        const int g = gt + j;
+        if (!warp_wait(&s_full[g & 1], (uint32_t)((g >> 1) & 1))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t tS = tmem + lane_base + (uint32_t)((g & 1) * kBN);
+        float sv[kBN];
+#pragma unroll
+        for (int c = 0; c < kBN / 32; ++c) tmem_ld32(tS + c * 32, *reinterpret_cast<float(*)[32]>(&sv[c * 32]));
+        const int pid_now = pid0;
+        pid0 = pid1;
+        pid1 = load_pid(j + 2);
+        tmem_wait_ld();
+        const int64_t key0 = (it.t_begin + j) * kBN;
+        // Only tiles that cross some row's last visible key (the causal diagonal, the
+        // context end, rows past the unit) pay for the mask: one compare per score.
+        const int64_t vis64 = last_key - key0;  // in-tile index of the row's last visible key
+        if (__any_sync(0xffffffffu, vis64 < kBN - 1)) {
+          const int vis = vis64 < -1 ? -1 : (int)vis64;
+#pragma unroll
+          for (int c = 0; c < kBN; ++c) sv[c] = c <= vis ? sv[c] : -INFINITY;
+        }
+        if (!p.dense) {  // holes: the 16-token groups of missing pages are masked
+          const uint32_t holes =
+              __ballot_sync(0xffffffffu, lane < kPagesPerTile && (pid_now < 0 || pid_now >= (int)p.P)) & 0xFu;
+          if (holes != 0) {
+#pragma unroll
+            for (int gg = 0; gg < kPagesPerTile; ++gg) {
+              if ((holes >> gg) & 1u) {
+#pragma unroll
+                for (int c = 0; c < 16; ++c) sv[gg * 16 + c] = -INFINITY;
+              }
+            }
+          }
+        }
+        // row max as a tree (8 independent chains), not one 64-long dependency chain
+        float mv[8];
+#pragma unroll
+        for (int x = 0; x < 8; ++x) mv[x] = sv[x];
+#pragma unroll
+        for (int c = 8; c < kBN; c += 8) {
+#pragma unroll
+          for (int x = 0; x < 8; ++x) mv[x] = fmaxf(mv[x], sv[c + x]);
+        }
+        const float mx = fmaxf(fmaxf(fmaxf(mv[0], mv[1]), fmaxf(mv[2], mv[3])), fmaxf(fmaxf(mv[4], mv[5]), fmaxf(mv[6], mv[7])));
+        const float mx_s = mx * sl2;
+        // lazy max: keep the old reference max unless the new one exceeds it by > 8
+        float m_ref = m;
+        bool rescale = false;
+        if (mx_s > -INFINITY && (m == -INFINITY || mx_s > m + kRescaleThreshold)) {
+          rescale = m != -INFINITY;
+          m_ref = mx_s;
+        }
+        const float mu = m_ref == -INFINITY ? 0.f : m_ref;
+        const float alpha = ex2_ftz(m - mu);  // 0 when m == -inf
+        // p = 2^(s * sl2 - mu) on packed pairs.  Most exponentials run on the MUFU unit;
+        // outside split tiles the pairs selected by kEmuPairs run on the FMA pipe instead
+        // (exp2_fma2), which keeps MUFU from setting the tile rate.
+        const float2 sl2v = make_float2(sl2, sl2), nmu = make_float2(-mu, -mu);
+        float2 acc[4];
+#pragma unroll
+        for (int x = 0; x < 4; ++x) acc[x] = make_float2(0.f, 0.f);
+        if (split) {
+#pragma unroll
+          for (int q = 0; q < kBN / 2; ++q) {
+            const float2 x2 = __ffma2_rn(make_float2(sv[2 * q], sv[2 * q + 1]), sl2v, nmu);
+            const float2 e = make_float2(ex2_ftz(x2.x), ex2_ftz(x2.y));
+            sv[2 * q] = e.x;
+            sv[2 * q + 1] = e.y;
+            acc[q & 3] = __fadd2_rn(acc[q & 3], e);
+          }
+        } else {
+#pragma unroll
+          for (int q = 0; q < kBN / 2; ++q) {
+            const float2 x2 = __ffma2_rn(make_float2(sv[2 * q], sv[2 * q + 1]), sl2v, nmu);
+            const float2 e = ((kEmuPairs >> q) & 1u) ? exp2_fma2<T>(x2) : make_float2(ex2_ftz(x2.x), ex2_ftz(x2.y));
+            sv[2 * q] = e.x;
+            sv[2 * q + 1] = e.y;
+            acc[q & 3] = __fadd2_rn(acc[q & 3], e);
+          }
+        }
+        const float2 a01 = __fadd2_rn(__fadd2_rn(acc[0], acc[1]), __fadd2_rn(acc[2], acc[3]));
+        // A row with no visible key yet keeps a zero sum (so it ends as zeros): exp2_fma2
+        // turns its -inf scores into 2^-125, not 0.  Next to a visible key's p >= 2^-8,
+        // 2^-125 is nothing.
+        const float rs = m_ref == -INFINITY ? 0.f : a01.x + a01.y;
+        lsum = (m == -INFINITY ? 0.f : lsum * alpha) + rs;
+        m = m_ref;
+        if (__any_sync(0xffffffffu, rescale)) {
+          // O must hold PV_{j-1} before it is rescaled
+          if (!warp_wait(o_done, (uint32_t)((g - 1) & 1))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const float f = rescale ? alpha : 1.f;
+#pragma unroll 1
+          for (int c = 0; c < kD / 32; ++c) {
+            float ov[32];
+            tmem_ld32(tO + lane_base + c * 32, ov);
+            tmem_wait_ld();
+#pragma unroll
+            for (int x = 0; x < 32; ++x) ov[x] *= f;
+            tmem_st32(tO + lane_base + c * 32, ov);
+          }
+        }
+        // P over S_j's columns: packed pairs, hi in columns [0, kBN/2), lo (bf16 split) after
+        {
+          uint32_t hi[32];
+#pragma unroll
+          for (int x = 0; x < 32; ++x) hi[x] = cvt_pack<T>(sv[2 * x], sv[2 * x + 1]);
+          tmem_st32u(tS, hi);
+          if (split) {
+            uint32_t lo[32];
+#pragma unroll
+            for (int x = 0; x < 32; ++x) {
+              // bf16 -> f32 is exact: the bf16 bits become the high half of the f32
+              const float h0 = __uint_as_float(hi[x] << 16), h1 = __uint_as_float(hi[x] & 0xFFFF0000u);
+              lo[x] = cvt_pack<T>(sv[2 * x] - h0, sv[2 * x + 1] - h1);
+            }
+            tmem_st32u(tS + kBN / 2, lo);
+          }
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&p_full[g & 1]);
+      }
+      if (!ok) break;
+      gt += n;
+      // Final O of the item: every PV done (item_done: one completion per item, so no
+      // parity aliasing with the per-tile o_done phases).
+      if (!warp_wait(item_done, iw & 1)) {
+        ok = false;
+        break;
+      }
+      ++iw;
+      tc_fence_after();
+      if (it.n_chunks_unit == 1) {
+        const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+#pragma unroll 1
+        for (int c1 = 0; c1 < kD; c1 += 64) {
+          float ov2[64];
+          tmem_ld32(tO + lane_base + c1, *reinterpret_cast<float(*)[32]>(&ov2[0]));
+          tmem_ld32(tO + lane_base + c1 + 32, *reinterpret_cast<float(*)[32]>(&ov2[32]));
+          tmem_wait_ld();
+          if (c1 + 64 == kD) {  // O read out: the next item's first PV may overwrite it
+            tc_fence_before();
+            mbar_arrive(o_free);
+          }
+          if (p.stage_out) {
+            stage32(ov2, c1, inv);
+            stage32(ov2 + 32, c1 + 32, inv);
+          } else if (row_ok) {
+            store32(orow, ov2, c1, inv);
+            store32(orow, ov2 + 32, c1 + 32, inv);
+          }
+        }
+        if (p.stage_out) flush_staged(it);
+      } else {
+        // Split-K: leave this chunk's (m, l) and unnormalised O rows in the workspace ...
+        const int64_t prow = (it.u * p.n_chunks + it.c) * p.rows_real + row;
+        if (row_ok) p.part_ml[prow] = make_float2(m, lsum);  // m = -inf: no visible key in this chunk
+#pragma unroll 1
+        for (int c1 = 0; c1 < kD; c1 += 64) {
+          float ov2[64];
+          tmem_ld32(tO + lane_base + c1, *reinterpret_cast<float(*)[32]>(&ov2[0]));
+          tmem_ld32(tO + lane_base + c1 + 32, *reinterpret_cast<float(*)[32]>(&ov2[32]));
+          tmem_wait_ld();
+          if (c1 + 64 == kD) {
+            tc_fence_before();
+            mbar_arrive(o_free);
+          }
+          if (row_ok) {
+            float4* po = reinterpret_cast<float4*>(p.part_o + prow * kD + c1);
+#pragma unroll
+            for (int x = 0; x < 16; ++x) po[x] = make_float4(ov2[4 * x], ov2[4 * x + 1], ov2[4 * x + 2], ov2[4 * x + 3]);
+          }
+        }
+        // ... and the unit's last chunk to finish merges them (log-sum-exp weights).
+        __threadfence();
+        named_barrier(1, 128);
+        if (row == 0) *(volatile int*)last_flag = atomicAdd(&p.counters[it.u], 1) == (int)it.n_chunks_unit - 1;
+        named_barrier(1, 128);
+        const bool merge = *(volatile int*)last_flag != 0;
+        named_barrier(1, 128);  // every thread has read the flag before it is reused
+        if (merge) {
+          __threadfence();
+          const int64_t base = it.u * p.n_chunks * p.rows_real + row;  // + cc * rows_real
+          float mxc = -INFINITY, lt = 0.f;
+          if (row_ok) {
+            for (int64_t cc = 0; cc < it.n_chunks_unit; ++cc)
+              mxc = fmaxf(mxc, __ldcg(&p.part_ml[base + cc * p.rows_real]).x);
+            for (int64_t cc = 0; cc < it.n_chunks_unit; ++cc) {
+              const float2 ml = __ldcg(&p.part_ml[base + cc * p.rows_real]);
+              if (ml.x != -INFINITY) lt += ml.y * exp2f(ml.x - mxc);
+            }
+            const float inv = lt > 0.f ? 1.f / lt : 0.f;
+#pragma unroll 1
+            for (int c0 = 0; c0 < kD; c0 += 32) {
+              float acc2[32];
+#pragma unroll
+              for (int x = 0; x < 32; ++x) acc2[x] = 0.f;
+              for (int64_t cc = 0; cc < it.n_chunks_unit; ++cc) {
+                const float2 ml = __ldcg(&p.part_ml[base + cc * p.rows_real]);
+                if (ml.x == -INFINITY) continue;
+                const float w = exp2f(ml.x - mxc);
+                const float4* po = reinterpret_cast<const float4*>(p.part_o + (base + cc * p.rows_real) * kD + c0);
+#pragma unroll
+                for (int x = 0; x < 8; ++x) {
+                  const float4 o4 = __ldcg(po + x);
+                  acc2[4 * x] += w * o4.x;
+                  acc2[4 * x + 1] += w * o4.y;
+                  acc2[4 * x + 2] += w * o4.z;
+                  acc2[4 * x + 3] += w * o4.w;
+                }
+              }
+              if (p.stage_out) stage32(acc2, c0, inv);
+              else store32(orow, acc2, c0, inv);
+            }
+          }
+          if (p.stage_out) flush_staged(it);
+          if (row == 0) p.counters[it.u] = 0;  // tickets start at zero for the next call
+        }
+      }
+    }
+    if (!ok) {
+      record_error(p.err, kDevErrFullWait);
+      *(volatile int*)abort_flag = 1;
     }
   }
 
   // ------------------------------------------------------------------ teardown
-  if (warp == 5 && lane == 0 && n_tiles > 0) {
+  if (warp == 5 && lane == 0) {
     if (!mbar_wait(mma_done, 0)) record_error(p.err, kDevErrMmaWait);
   }
   tc_fence_before();
@@ -910,6 +1012,14 @@ __global__ void __launch_bounds__(kThreads, 2)
   tc_fence_after();
   if (warp == 5) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+  // the last CTA to leave resets the work counter for the next call
+  if (threadIdx.x == 0 && p.work_counter != nullptr) {
+    __threadfence();
+    if (atomicAdd(p.exit_counter, 1) == (int)gridDim.x - 1) {
+      *p.work_counter = 0;
+      *p.exit_counter = 0;
+    }
   }
 }
 
@@ -980,7 +1090,7 @@ Sm100Plan plan_sm100(const PagedArgs& a, bool sizing_only) {
   // Split-K over keys for grouped paged calls (dense callers pass no workspace): aim at
   // a few CTAs per SM slot if every sequence were max_pages long; units whose context is
   // shorter leave their later chunks empty (those CTAs return at once).
-  if (plan.grouped && !a.dense && plan.n_units <= (int64_t)(kSm100CounterBytes / sizeof(int))) {
+  if (plan.grouped && !a.dense && plan.n_units <= kMaxTicketUnits) {
     int64_t ct = env_int("NVM_SM100_CHUNK_TILES", 0);
     if (ct <= 0) {
       const int64_t target = 148 * 2 * 4;
@@ -994,6 +1104,9 @@ Sm100Plan plan_sm100(const PagedArgs& a, bool sizing_only) {
   }
   if (plan.n_units * plan.n_chunks > INT32_MAX) return plan;
   plan.ws_bytes = 0;
+  // Paged calls take their work items from a counter in the workspace (dense callers
+  // pass none and walk items by CTA index).
+  if (!a.dense) plan.ws_bytes = kSm100CounterBytes;
   if (plan.n_chunks > 1) {
     const size_t ml = (size_t)(plan.n_units * plan.n_chunks * plan.rows_real) * sizeof(float2);
     plan.ws_bytes = kSm100CounterBytes + ((ml + 255) & ~size_t(255)) +
@@ -1049,7 +1162,11 @@ int launch_sm100(const PagedArgs& a, const Sm100Plan& plan, void* ws, cudaStream
   p.g = a.Hq / a.Hkv;
   p.M_rows = plan.M_rows; p.n_outer = plan.n_outer; p.n_units = plan.n_units;
   p.ct = plan.ct; p.n_chunks = plan.n_chunks; p.rows_real = plan.rows_real;
-  p.prefetch = (int)env_int("NVM_SM100_PREFETCH", 0);
+  p.n_items = plan.n_units * plan.n_chunks;
+  if (ws != nullptr && plan.ws_bytes > 0) {
+    p.work_counter = reinterpret_cast<int*>(ws) + (kSm100CounterBytes / sizeof(int) - 2);
+    p.exit_counter = p.work_counter + 1;
+  }
   if (plan.n_chunks > 1) {
     uint8_t* w = static_cast<uint8_t*>(ws);
     p.counters = reinterpret_cast<int*>(w);
@@ -1060,7 +1177,20 @@ int launch_sm100(const PagedArgs& a, const Sm100Plan& plan, void* ws, cudaStream
     p.part_o = reinterpret_cast<float*>(w);
   }
 
-  const dim3 grid((unsigned)(plan.n_units * plan.n_chunks));
+  // Grouped (decode-like) calls: persistent grid of two CTAs per SM taking items from the
+  // work counter, so skewed contexts balance and item prologues overlap.  Prefill: one CTA
+  // per item (the hardware scheduler balances the heavy-first causal tiles), which lets
+  // the epilogue stage O in shared memory for bulk tensor stores.
+  int64_t ctas = p.n_items;
+  const int64_t persistent = env_int("NVM_SM100_PERSISTENT", plan.grouped ? 1 : 0);
+  if (persistent != 0) {
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (ctas > 2 * (int64_t)sms) ctas = 2 * (int64_t)sms;
+  }
+  p.stage_out = ctas == p.n_items ? 1 : 0;
+  if (p.stage_out) p.work_counter = p.exit_counter = nullptr;  // one item per CTA: item = blockIdx.x
+  const dim3 grid((unsigned)ctas);
   if (a.kv_dtype == NVM_F16) return launch_typed<__half>(grid, tq, tk, tv, to, p, s);
   return launch_typed<__nv_bfloat16>(grid, tq, tk, tv, to, p, s);
 }

@@ -1073,7 +1073,7 @@ Sm100Plan plan_sm100(const PagedArgs& a, bool sizing_only) {
     plan.grouped = 0;
     plan.M_rows = a.L;
     plan.n_outer = a.B * a.Hq;
-  } else if (a.L > 1 && g * a.L >= min_rows && env_int("NVM_SM100_GROUPED", 1) != 0) {
+  } else if ((a.L > 1 || min_rows <= g) && g * a.L >= min_rows && env_int("NVM_SM100_GROUPED", 1) != 0) {
     plan.grouped = 1;
     plan.M_rows = g * a.L;
     plan.n_outer = a.B * a.Hkv;

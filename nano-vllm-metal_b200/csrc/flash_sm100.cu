@@ -55,7 +55,8 @@ constexpr float kRescaleThreshold = 8.0f;  // log2(256)
 // Split-K tickets: a fixed region at the start of the workspace (one int per unit); its
 // last two ints are the work-item counter and the exit counter of the persistent grid.
 constexpr size_t kSm100CounterBytes = 1u << 20;
-constexpr int64_t kMaxTicketUnits = (int64_t)(kSm100CounterBytes / sizeof(int)) - 2;
+constexpr int64_t kMaxTicketUnits = (int64_t)(kSm100CounterBytes / sizeof(int)) - 3;
+constexpr int kPlanBins = 1024;  // tile-count bins of the plan's counting sort
 
 int64_t env_int(const char* name, int64_t dflt) {
   const char* v = std::getenv(name);
@@ -88,6 +89,8 @@ struct Sm100Params {
   int64_t ct, n_chunks, rows_real;
   int64_t n_items;    // n_units * n_chunks work items
   int* work_counter;  // next item (in the workspace); null: item = blockIdx.x + k * gridDim.x
+  const int* item_list;   // items with work, largest first (plan kernel); null: every item index
+  const int* item_count;  // length of item_list
   int stage_out;      // one item per CTA: O leaves through shared memory and bulk tensor stores
   int* exit_counter;  // CTAs done; the last one resets both counters
   int* counters;
@@ -271,7 +274,10 @@ struct Item {
 
 __device__ __forceinline__ Item decode_item(const Sm100Params& p, int64_t item) {
   Item it;
-  it.c = item / p.n_units;  // chunk-major: every unit's chunk 0 comes before any chunk 1
+  // Chunk-major, last chunk first: a chunk c >= 1 exists only for long units and is then
+  // full-size (except each unit's last), so handing out high chunks first and the mixed
+  // chunk-0 items (short units included) last approximates longest-first scheduling.
+  it.c = p.n_chunks - 1 - item / p.n_units;
   it.u = item % p.n_units;
   const int64_t rt = p.n_row_tiles - 1 - (it.u % p.n_row_tiles);  // heavy (late, causal) row tiles first
   it.n = it.u / p.n_row_tiles;  // flat (b, q head), or (b, kv head) when grouped
@@ -402,6 +408,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int leader_lane = __ffs(__ballot_sync(0xffffffffu, leader)) - 1;
     int gk = 0, gv = 0;  // K / V tiles issued by this CTA so far
     int kq = 0, iw = 0;      // items published, items with keys
+    int64_t n_fetched = 0;   // item indices taken (static order: blockIdx.x + k * gridDim.x)
     bool ok = true;
     while (ok) {
       const int slot = kq & 3;
@@ -409,15 +416,34 @@ __global__ void __launch_bounds__(kThreads, 2)
         ok = false;
         break;
       }
+      // Next item with work: chunks past a unit's last key are skipped here, without
+      // taking a ring slot (the consumers would otherwise drain them only after their
+      // current item, and the next real item's loads would start that late).
       int64_t item;
-      if (p.work_counter != nullptr) {
-        int v = 0;
-        if (leader) v = atomicAdd(p.work_counter, 1);
-        item = __shfl_sync(0xffffffffu, v, leader_lane);
-      } else {
-        item = (int64_t)blockIdx.x + (int64_t)kq * gridDim.x;
+      Item it;
+      for (;;) {
+        if (p.item_list != nullptr) {
+          int v = 0;
+          if (leader) {
+            const int k = atomicAdd(p.work_counter, 1);
+            v = k < *p.item_count ? __ldcg(&p.item_list[k]) : INT32_MAX;
+          }
+          item = __shfl_sync(0xffffffffu, v, leader_lane);
+        } else if (p.work_counter != nullptr) {
+          int v = 0;
+          if (leader) v = atomicAdd(p.work_counter, 1);
+          item = __shfl_sync(0xffffffffu, v, leader_lane);
+        } else {
+          item = (int64_t)blockIdx.x + (int64_t)n_fetched * gridDim.x;
+        }
+        ++n_fetched;
+        if (item >= p.n_items) {
+          item = -1;
+          break;
+        }
+        it = decode_item(p, item);
+        if (it.valid) break;
       }
-      if (item >= p.n_items) item = -1;
       if (leader) {
         *(volatile int64_t*)&item_ring[slot] = item;
         mbar_arrive(&item_full[slot]);
@@ -425,8 +451,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       __syncwarp();
       ++kq;
       if (item < 0) break;
-      const Item it = decode_item(p, item);
-      if (it.n_tiles == 0) continue;
+      if (it.n_tiles == 0) continue;  // no key: the softmax warps write zero rows
       const int kvh_i = (int)it.kvh, b_i = (int)it.b;
       const int32_t* bt_row = p.dense ? nullptr : p.block_table + it.b * p.mp;
       if (iw > 0 && !warp_wait(q_empty, (iw - 1) & 1)) {
@@ -1023,6 +1048,38 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
 }
 
+// Work list for the persistent grid: every item with work, ordered by tile count, largest
+// first (a counting sort; sizes >= kPlanBins - 1 share the first bin), so the dynamic
+// fetch approximates longest-processing-time-first scheduling.  One CTA.
+__global__ void __launch_bounds__(1024) sm100_plan_kernel(const Sm100Params p, int* list, int* count) {
+  __shared__ int hist[kPlanBins];
+  for (int i = threadIdx.x; i < kPlanBins; i += blockDim.x) hist[i] = 0;
+  __syncthreads();
+  for (int64_t item = threadIdx.x; item < p.n_items; item += blockDim.x) {
+    const Item it = decode_item(p, item);
+    if (!it.valid) continue;
+    const int bin = kPlanBins - 1 - (it.n_tiles < kPlanBins - 1 ? it.n_tiles : kPlanBins - 1);
+    atomicAdd(&hist[bin], 1);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int acc = 0;
+    for (int b = 0; b < kPlanBins; ++b) {
+      const int c = hist[b];
+      hist[b] = acc;
+      acc += c;
+    }
+    *count = acc;
+  }
+  __syncthreads();
+  for (int64_t item = threadIdx.x; item < p.n_items; item += blockDim.x) {
+    const Item it = decode_item(p, item);
+    if (!it.valid) continue;
+    const int bin = kPlanBins - 1 - (it.n_tiles < kPlanBins - 1 ? it.n_tiles : kPlanBins - 1);
+    list[atomicAdd(&hist[bin], 1)] = (int)item;
+  }
+}
+
 // One opt-in to the dynamic shared memory size per kernel instantiation and device.
 template <typename T>
 int launch_typed(dim3 grid, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
@@ -1046,6 +1103,26 @@ int launch_typed(dim3 grid, const CUtensorMap& tq, const CUtensorMap& tk, const 
 }
 
 }  // namespace
+
+// Workspace of a paged call: tickets + counters (1 MiB), the work list, then the split-K
+// partials (m, l) and O.
+struct WsOffsets {
+  size_t list, ml, o, total;
+};
+WsOffsets sm100_ws_offsets(const Sm100Plan& plan) {
+  auto al = [](size_t x) { return (x + 255) & ~size_t(255); };
+  WsOffsets w{};
+  const size_t items = (size_t)(plan.n_units * plan.n_chunks);
+  w.list = kSm100CounterBytes;
+  w.ml = w.list + al(items * sizeof(int));
+  w.o = w.ml;
+  w.total = w.ml;
+  if (plan.n_chunks > 1) {
+    w.o = w.ml + al(items * (size_t)plan.rows_real * sizeof(float2));
+    w.total = w.o + items * (size_t)plan.rows_real * kD * sizeof(float);
+  }
+  return w;
+}
 
 Sm100Plan plan_sm100(const PagedArgs& a, bool sizing_only) {
   Sm100Plan plan{};
@@ -1106,12 +1183,7 @@ Sm100Plan plan_sm100(const PagedArgs& a, bool sizing_only) {
   plan.ws_bytes = 0;
   // Paged calls take their work items from a counter in the workspace (dense callers
   // pass none and walk items by CTA index).
-  if (!a.dense) plan.ws_bytes = kSm100CounterBytes;
-  if (plan.n_chunks > 1) {
-    const size_t ml = (size_t)(plan.n_units * plan.n_chunks * plan.rows_real) * sizeof(float2);
-    plan.ws_bytes = kSm100CounterBytes + ((ml + 255) & ~size_t(255)) +
-                    (size_t)(plan.n_units * plan.n_chunks * plan.rows_real) * kD * sizeof(float);
-  }
+  if (!a.dense) plan.ws_bytes = sm100_ws_offsets(plan).total;
   plan.eligible = true;
   return plan;
 }
@@ -1167,14 +1239,12 @@ int launch_sm100(const PagedArgs& a, const Sm100Plan& plan, void* ws, cudaStream
     p.work_counter = reinterpret_cast<int*>(ws) + (kSm100CounterBytes / sizeof(int) - 2);
     p.exit_counter = p.work_counter + 1;
   }
+  const WsOffsets wo = sm100_ws_offsets(plan);
   if (plan.n_chunks > 1) {
     uint8_t* w = static_cast<uint8_t*>(ws);
     p.counters = reinterpret_cast<int*>(w);
-    w += kSm100CounterBytes;
-    p.part_ml = reinterpret_cast<float2*>(w);
-    const size_t ml = (size_t)(plan.n_units * plan.n_chunks * plan.rows_real) * sizeof(float2);
-    w += (ml + 255) & ~size_t(255);
-    p.part_o = reinterpret_cast<float*>(w);
+    p.part_ml = reinterpret_cast<float2*>(w + wo.ml);
+    p.part_o = reinterpret_cast<float*>(w + wo.o);
   }
 
   // Grouped (decode-like) calls: persistent grid of two CTAs per SM taking items from the
@@ -1190,6 +1260,15 @@ int launch_sm100(const PagedArgs& a, const Sm100Plan& plan, void* ws, cudaStream
   }
   p.stage_out = ctas == p.n_items ? 1 : 0;
   if (p.stage_out) p.work_counter = p.exit_counter = nullptr;  // one item per CTA: item = blockIdx.x
+  if (p.work_counter != nullptr && env_int("NVM_SM100_PLAN", 1) != 0) {
+    int* list = reinterpret_cast<int*>(static_cast<uint8_t*>(ws) + wo.list);
+    int* count = p.work_counter - 1;
+    p.item_list = list;
+    p.item_count = count;
+    sm100_plan_kernel<<<1, 1024, 0, s>>>(p, list, count);
+    const int st2 = check_cuda(cudaGetLastError(), "paged_attention: sm100 plan kernel launch");
+    if (st2 != NVM_OK) return st2;
+  }
   const dim3 grid((unsigned)ctas);
   if (a.kv_dtype == NVM_F16) return launch_typed<__half>(grid, tq, tk, tv, to, p, s);
   return launch_typed<__nv_bfloat16>(grid, tq, tk, tv, to, p, s);

@@ -279,8 +279,10 @@ __device__ __forceinline__ Item decode_item(const Sm100Params& p, int64_t item) 
   // chunk-0 items (short units included) last approximates longest-first scheduling.
   it.c = p.n_chunks - 1 - item / p.n_units;
   it.u = item % p.n_units;
-  const int64_t rt = p.n_row_tiles - 1 - (it.u % p.n_row_tiles);  // heavy (late, causal) row tiles first
-  it.n = it.u / p.n_row_tiles;  // flat (b, q head), or (b, kv head) when grouped
+  // Row-tile-major, heavy (late, causal) row tiles first across all heads: dispatch in
+  // item order is then longest-first.
+  const int64_t rt = p.n_row_tiles - 1 - it.u / p.n_outer;
+  it.n = it.u % p.n_outer;  // flat (b, q head), or (b, kv head) when grouped
   it.b = p.grouped ? it.n / p.Hkv : it.n / p.Hq;
   it.kvh = p.grouped ? it.n % p.Hkv : (it.n % p.Hq) / p.g;
   it.ctx = p.dense ? p.dense_ctx : (int64_t)p.context_lens[it.b];

@@ -100,3 +100,27 @@ def test_grouped_matches_mma_path(cuda, monkeypatch):
     monkeypatch.setenv("NVM_SM100_GROUPED", "0")
     b = _run(prob)
     torch.testing.assert_close(a, b, atol=2e-3, rtol=1e-2)
+
+
+def test_grouped_dense_many_units(cuda, oracle):
+    """Dense few-token calls with more units than the persistent grid (two CTAs per SM):
+    CTAs walk the units by index and store rows directly."""
+    gen = torch.Generator().manual_seed(31)
+    q = torch.randn(200, 16, 4, 128, generator=gen).bfloat16()
+    k = torch.randn(200, 2, 96, 128, generator=gen).bfloat16()
+    v = torch.randn(200, 2, 96, 128, generator=gen).bfloat16()
+    out = flash_attention(q.cuda(), k.cuda(), v.cuda(), mask="causal", out_dtype=torch.float32)
+    ref = oracle.flash_attention_ref(q.float().numpy(), k.float().numpy(), v.float().numpy(), mask="causal",
+                                     nthreads=8)
+    assert_close(out, ref, TOL16)
+    assert nv.device_error(cuda) == 0
+
+
+def test_grouped_fp16_and_out_dtypes(cuda, oracle):
+    gen = torch.Generator().manual_seed(41)
+    prob = random_paged_problem(gen, 3, 16, 2, 4, 128, 16, torch.float16, 4, 1200, holes=True)
+    for od in (torch.float32, torch.float16):
+        out = _run(prob, out_dtype=od)
+        assert out.dtype == od
+        assert_close(out.float(), oracle_paged(oracle, prob), TOL16)
+    assert nv.device_error(cuda) == 0

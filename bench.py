@@ -14,8 +14,9 @@ GPUs every rank owns Hkv/N kv heads and their pools (KV-head sharding, no
 collective in the timed region); ``value`` = logical K/V+Q/O+metadata bytes of all
 ranks / max-over-ranks time (strong scaling: the job is fixed as N grows).
 
-Secondary lines (N=1 only) time configs 1, 4, 5 (decode GB/s) and 2a / 2b (prefill
-TFLOPS) one launch at a time with an L2 flush between launches.
+Secondary lines (N=1 only) time configs 1, 4, 5 (decode GB/s), 2a / 2b (prefill
+TFLOPS) and the fused q/k-norm + RoPE + K/V write at the 2a token count (GB/s) one
+launch at a time with an L2 flush between launches.
 """
 
 from __future__ import annotations
@@ -383,7 +384,77 @@ def secondary_results(peaks: dict, device) -> list[dict]:
                         value=round(tf, 1), unit="TFLOP/s", ms=round(ms, 4),
                         roofline_frac=round(tf / peaks["bf16"], 4)))
         del w
+    res.extend(qk_prep_results(peaks, device, flush))
     return res
+
+
+def qk_prep_bytes(T: int, Hq: int, Hkv: int, D: int, kv_bytes: int, scale_bytes: int) -> int:
+    """Algorithmic bytes of one fused q/k-norm + RoPE + K/V write over T tokens: read q, k,
+    v rows once, write q once and K/V (+ int8 scales) once, one fp32 cos and sin row,
+    the position and the slot of every token (the norm weights are 2 * D elements)."""
+    per_tok = (Hq + 2 * Hkv) * D * 2 + Hq * D * 2 + 2 * Hkv * (D * kv_bytes + scale_bytes) + D * 4 + 4 + 8
+    return T * per_tok + 2 * D * 2
+
+
+def qk_prep_results(peaks: dict, device, flush, B: int = 4, iters: int = 20, warmup: int = 3,
+                    kinds=("bf16", "int8")) -> list[dict]:
+    """Secondary lines: the fused step at the config-2a token count (4 x 2048 tokens,
+    Qwen3-4B heads 32 / 8, d 128, bf16) writing into bf16 and into int8 page pools."""
+    from nano_vllm_b200.layers.qk_prep import qk_norm_rope_write
+    from nano_vllm_b200.layers.rotary_embedding import RoPE
+
+    res = []
+    L, Hq, Hkv, D, ps = 2048, 32, 8, 128, 16
+    T = B * L
+    gen = torch.Generator(device=device)
+    gen.manual_seed(9)
+    qkv = torch.randn(B, L, (Hq + 2 * Hkv) * D, generator=gen, device=device).bfloat16()
+    q = qkv[..., :Hq * D].view(B, L, Hq, D)
+    k = qkv[..., Hq * D:(Hq + Hkv) * D].view(B, L, Hkv, D)
+    v = qkv[..., (Hq + Hkv) * D:].view(B, L, Hkv, D)
+    wq = torch.rand(D, generator=gen, device=device).bfloat16() + 0.5
+    wk = torch.rand(D, generator=gen, device=device).bfloat16() + 0.5
+    rope = RoPE(D, 40960, 1000000, device=device)
+    pos = (torch.arange(L, device=device, dtype=torch.int32) + 512).repeat(B, 1)
+    P = T // ps
+    slots = torch.randperm(P * ps, generator=gen, device=device)[:T]
+    out = torch.empty(B, Hq, L, D, dtype=torch.bfloat16, device=device)
+    for kv in kinds:
+        kv_dtype = torch.int8 if kv == "int8" else torch.bfloat16
+        kp = torch.zeros(P, Hkv, ps, D, dtype=kv_dtype, device=device)
+        vp = torch.zeros_like(kp)
+        ks = torch.ones(P, Hkv, ps, 1, dtype=torch.bfloat16, device=device) if kv == "int8" else None
+        vs = None if ks is None else ks.clone()
+        nbytes = qk_prep_bytes(T, Hq, Hkv, D, 1 if kv == "int8" else 2, 2 if kv == "int8" else 0)
+        ms = statistics.median(time_launches(
+            lambda: qk_norm_rope_write(q, k, v, wq, wk, rope, pos, kp, vp, slots, eps=1e-6, key_scales=ks,
+                                       value_scales=vs, out=out), iters, warmup, flush))
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        res.append(dict(workload=f"qk-norm+RoPE+KV write, {T} tokens (config2a shape), {kv} pages",
+                        metric="qk-prep GB/s", value=round(gbs, 1), unit="GB/s", ms=round(ms, 4),
+                        bytes=nbytes, roofline_frac=round(gbs / peaks["hbm"], 4), l2="flushed"))
+        del kp, vp, ks, vs
+    return res
+
+
+def run_qkprep(args):
+    """The fused q/k-norm + RoPE + K/V write alone (bf16 pools), 4 x 2048 tokens unless
+    --batch says otherwise; one JSON line."""
+    from nano_vllm_b200 import _native as nv
+
+    device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(device)
+    peaks = measured_peaks()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    r = qk_prep_results(peaks, device, flush, B=args.batch or 4, iters=args.steps, warmup=args.warmup,
+                        kinds=("bf16",))[0]
+    line = {"metric": r["metric"], "value": r["value"], "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": r["ms"], "higher_is_better": True, "dtype": "bf16",
+            "config": {"workload": r["workload"], "l2": "flushed between launches"},
+            "roofline": {"bound": "hbm", "achieved": r["value"], "peak": peaks["hbm"], "unit": "GB/s",
+                         "frac": r["roofline_frac"], "peak_source": peaks["src"], "algorithmic_bytes": r["bytes"]},
+            "device_error_word": nv.device_error(device)}
+    print(json.dumps(line), flush=True)
 
 
 def run_prefill(args):
@@ -422,6 +493,8 @@ def run_ours(args):
 
     if args.config == "c2a":
         return run_prefill(args)
+    if args.config == "qkprep":
+        return run_qkprep(args)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -570,7 +643,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["c1", "c2a", "c3", "c4", "c5"], default="c3")
+    ap.add_argument("--config", choices=["c1", "c2a", "c3", "c4", "c5", "qkprep"], default="c3")
     ap.add_argument("--batch", type=int, default=None, help="override the config's batch (small profiling cases)")
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")

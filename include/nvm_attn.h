@@ -74,7 +74,8 @@ const char* nvm_version(void);
  * device, optionally clears it, and returns it (0 = no error).  The first code
  * recorded stays: 1 a wait for a tile to land expired, 2 a wait for a free stage,
  * 3 draining in-flight copies, 4 tensor-memory allocation, 5 tensor-core completion,
- * 6 dynamic shared memory was not 1024-byte aligned (that kernel computed nothing).
+ * 6 dynamic shared memory was not 1024-byte aligned (that kernel computed nothing),
+ * 7 a device-side index (a rope position or a slot) was outside its table (row skipped).
  */
 int nvm_device_error(void* stream, int clear);
 
@@ -188,6 +189,36 @@ int nvm_reshape_and_cache(const void* k, const void* v, int in_dtype, int64_t st
                           void* k_scales, void* v_scales, int scale_dtype,
                           const int64_t* slot_mapping, int64_t T, int64_t Hkv, int64_t D,
                           int64_t P, int64_t page_size, void* stream);
+
+/* ------------------------------------------------------------------------- */
+/* Fused per-layer preparation: q/k RMSNorm + RoPE + K/V scatter-write        */
+/* ------------------------------------------------------------------------- */
+/*
+ * Replaces the steps of Qwen3Attention.__call__ between the QKV projection and the
+ * attention call (src/nano_vllm_metal/models/qwen3.py:100-116): q_norm/k_norm
+ * (layers/layernorm.py:4-14, RMSNorm over the head dim with weight, eps), RoPE on q and
+ * k (layers/rotary_embedding.py:74-124; halves rotated, or interleaved pairs when
+ * traditional != 0) and the pool write of cache.update_and_fetch_paged
+ * (cache/paged.py:160-195, int8 through _quantize_page_slice, paged.py:152-158).
+ *   q [T, Hq, D], k/v [T, Hkv, D] (dtype f16/bf16; q_stride_t / kv_stride_t elements
+ *   between tokens, heads contiguous); q_norm_weight / k_norm_weight [D] (dtype);
+ *   cos_table / sin_table [table_rows, D/2] fp32 (position p, angle index i);
+ *   positions [T] int32 (the token's position = request offset + index in the chunk);
+ *   q_out: the normalised, rotated q, [T, Hq, D], or [T/q_out_L, Hq, q_out_L, D] when
+ *   q_out_L > 0 (the [B, Hq, L, D] layout paged_attention takes);
+ *   K (normalised, rotated) and V (as given) go to the pages at slot_mapping[t]
+ *   (page_id * page_size + offset; negative = skip), copied or int8-quantised as
+ *   nvm_reshape_and_cache does.  D must be 64 or 128.  Rounding follows the reference:
+ *   the norm result and the rotation result are each rounded to dtype, the rotation is
+ *   computed in fp32 from the rounded norm result.
+ */
+int nvm_qk_norm_rope_write(const void* q, const void* k, const void* v, int dtype, int64_t q_stride_t,
+                           int64_t kv_stride_t, const void* q_norm_weight, const void* k_norm_weight,
+                           float eps, const float* cos_table, const float* sin_table, int64_t table_rows,
+                           int traditional, const int32_t* positions, void* q_out, int64_t q_out_L,
+                           void* k_pages, void* v_pages, int kv_dtype, void* k_scales, void* v_scales,
+                           int scale_dtype, const int64_t* slot_mapping, int64_t T, int64_t Hq,
+                           int64_t Hkv, int64_t D, int64_t P, int64_t page_size, void* stream);
 
 /* ------------------------------------------------------------------------- */
 /* Device-side page allocation for one batched append                         */

@@ -23,6 +23,7 @@ enum DeviceError : int {
   kDevErrTmemAlloc = 4,   // tensor-memory allocation wait expired
   kDevErrMmaWait = 5,     // tensor-core completion wait expired
   kDevErrSmemAlign = 6,   // dynamic shared memory not 1024-byte aligned (kernel did nothing)
+  kDevErrBadIndex = 7,    // a device-side index (position, slot) outside its table; the row was skipped
 };
 
 // Every spin-wait gives up after this many nanoseconds of %globaltimer.

@@ -369,6 +369,43 @@ void oracle_flash_attention(const float* q, const float* k, const float* v, cons
   }
 }
 
+/* raw store of one element of dtype (F32 / F16 bits / BF16 bits), RNE */
+static inline void store_elem(void* base, int64_t idx, int dtype, float f) {
+  if (dtype == OR_F32)
+    ((float*)base)[idx] = f;
+  else if (dtype == OR_F16)
+    ((uint16_t*)base)[idx] = f32_to_f16(f);
+  else
+    ((uint16_t*)base)[idx] = f32_to_bf16(f);
+}
+
+/* value after a round trip through dtype (identity for F32) */
+static inline float round_to(float f, int dtype) {
+  if (dtype == OR_F16) return f16_to_f32(f32_to_f16(f));
+  if (dtype == OR_BF16) return bf16_to_f32(f32_to_bf16(f));
+  return f;
+}
+
+/* One row of _quantize_page_slice (paged.py:152-158): amax in fp32, s = amax / 127
+ * (1 when amax == 0), q = clip(round_half_even(x / s), -127, 127); scale stored in
+ * scale_dtype at index sidx. */
+static void quantize_row(const float* x, int64_t D, int8_t* q_out, void* scale_out, int64_t sidx,
+                         int scale_dtype) {
+  float amax = 0.0f;
+  for (int64_t d = 0; d < D; d++) {
+    const float a = fabsf(x[d]);
+    if (a > amax) amax = a;
+  }
+  const float s = amax > 0.0f ? amax / 127.0f : 1.0f;
+  for (int64_t d = 0; d < D; d++) {
+    float y = rintf(x[d] / s);
+    if (y < -127.0f) y = -127.0f;
+    if (y > 127.0f) y = 127.0f;
+    q_out[d] = (int8_t)y;
+  }
+  store_elem(scale_out, sidx, scale_dtype, s);
+}
+
 /*
  * TinyKvPagedPool._quantize_page_slice -- src/nano_vllm_metal/cache/paged.py:152-158.
  * x [rows, D] of in_dtype (F32/F16/BF16).  Per row: amax = max|x| in fp32,
@@ -378,24 +415,118 @@ void oracle_flash_attention(const float* q, const float* k, const float* v, cons
  */
 void oracle_quantize_int8(const void* x, int in_dtype, int64_t rows, int64_t D, int8_t* q_out,
                           void* scale_out) {
+  float* row = (float*)malloc((size_t)D * sizeof(float));
   for (int64_t r = 0; r < rows; r++) {
-    float amax = 0.0f;
-    for (int64_t d = 0; d < D; d++) {
-      const float a = fabsf(load_elem(x, r * D + d, in_dtype));
-      if (a > amax) amax = a;
-    }
-    const float s = amax > 0.0f ? amax / 127.0f : 1.0f;
-    for (int64_t d = 0; d < D; d++) {
-      float y = rintf(load_elem(x, r * D + d, in_dtype) / s);
-      if (y < -127.0f) y = -127.0f;
-      if (y > 127.0f) y = 127.0f;
-      q_out[r * D + d] = (int8_t)y;
-    }
-    if (in_dtype == OR_F32)
-      ((float*)scale_out)[r] = s;
-    else if (in_dtype == OR_F16)
-      ((uint16_t*)scale_out)[r] = f32_to_f16(s);
-    else
-      ((uint16_t*)scale_out)[r] = f32_to_bf16(s);
+    for (int64_t d = 0; d < D; d++) row[d] = load_elem(x, r * D + d, in_dtype);
+    quantize_row(row, D, q_out + r * D, scale_out, r, in_dtype);
   }
+  free(row);
+}
+
+/* sum of x[i]^2 in the order of a 32-lane tree: lane l holds EH = D/64 elements of each
+ * half of the row (x[l*EH .. l*EH+EH-1] and x[D/2 + l*EH ..]) and sums their squares in
+ * that order, then five butterfly steps (offsets 16, 8, 4, 2, 1) add the partner lane's
+ * partial.  Every order is a valid evaluation of mean(x^2); this one is the order of the
+ * product kernel, so the oracle agrees with it bit for bit.  D not a multiple of 64 sums
+ * sequentially. */
+static float sum_squares(const float* x, int64_t D) {
+  if (D % 64 != 0) {
+    float ss = 0.0f;
+    for (int64_t d = 0; d < D; d++) ss = ss + x[d] * x[d];
+    return ss;
+  }
+  const int64_t EH = D / 64, half = D / 2;
+  float part[32];
+  for (int l = 0; l < 32; l++) {
+    float ss = 0.0f;
+    for (int64_t e = 0; e < EH; e++) ss = ss + x[l * EH + e] * x[l * EH + e];
+    for (int64_t e = 0; e < EH; e++) ss = ss + x[half + l * EH + e] * x[half + l * EH + e];
+    part[l] = ss;
+  }
+  for (int off = 16; off >= 1; off >>= 1) {
+    float nxt[32];
+    for (int l = 0; l < 32; l++) nxt[l] = part[l] + part[l ^ off];
+    memcpy(part, nxt, sizeof(part));
+  }
+  return part[0];
+}
+
+/*
+ * The per-layer step between the QKV projection and attention in
+ * Qwen3Attention.__call__ -- src/nano_vllm_metal/models/qwen3.py:100-116:
+ *   1. q_norm / k_norm (layers/layernorm.py:4-14, mx.fast.rms_norm): per head row,
+ *      x * (1 / sqrt(mean(x^2) + eps)) * weight in fp32, result rounded to dtype.
+ *      wq == NULL skips the norm (RoPE alone, as the reference's RoPE tests run it).
+ *   2. RoPE (layers/rotary_embedding.py:74-124, custom backend): cos/sin rows of the
+ *      fp32 tables at the token's position; halves (x1 = x[:D/2], x2 = x[D/2:]) or,
+ *      when traditional, interleaved pairs (x[2i], x[2i+1]); real = x1*c - x2*s,
+ *      imag = x1*s + x2*c with every product and sum rounded to fp32 (dtype inputs
+ *      promote to fp32), result rounded to dtype.
+ *   3. cache.update_and_fetch_paged (cache/kv_cache.py:113-173 -> cache/paged.py:
+ *      160-195): rotated K and raw V written at slot = page_id * page_size + offset
+ *      of pools [P, Hkv, page_size, D]; int8 pools through _quantize_page_slice.
+ * q, k, v [T, H, D] of dtype; q_out [T, Hq, D] of dtype.  Slots < 0 are skipped.
+ * Returns 0, or 1 for a position outside the table / a page id >= P (that row is
+ * skipped, as the product kernel does).
+ */
+int oracle_qk_norm_rope_write(const void* q, const void* k, const void* v, int dtype, const void* wq,
+                              const void* wk, float eps, const float* cos_t, const float* sin_t,
+                              int64_t table_rows, int traditional, const int32_t* pos, void* q_out,
+                              void* k_pages, void* v_pages, int kv_dtype, void* k_scales, void* v_scales,
+                              int scale_dtype, const int64_t* slots, int64_t T, int64_t Hq, int64_t Hkv,
+                              int64_t D, int64_t P, int64_t page_size) {
+  const int64_t half = D / 2;
+  int err = 0;
+  float* x = (float*)malloc((size_t)D * sizeof(float));
+  float* y = (float*)malloc((size_t)D * sizeof(float));
+  for (int64_t t = 0; t < T; t++) {
+    for (int64_t r = 0; r < Hq + 2 * Hkv; r++) {
+      const int is_q = r < Hq, is_k = !is_q && r < Hq + Hkv;
+      const int64_t h = is_q ? r : (is_k ? r - Hq : r - Hq - Hkv);
+      const void* src = is_q ? q : (is_k ? k : v);
+      const int64_t base = (t * (is_q ? Hq : Hkv) + h) * D;
+      for (int64_t d = 0; d < D; d++) x[d] = load_elem(src, base + d, dtype);
+      if (is_q || is_k) {
+        const void* w = is_q ? wq : wk;
+        if (w != NULL) {
+          const float inv = 1.0f / sqrtf(sum_squares(x, D) / (float)D + eps);
+          for (int64_t d = 0; d < D; d++) x[d] = round_to(x[d] * inv * load_elem(w, d, dtype), dtype);
+        }
+        if (pos[t] < 0 || pos[t] >= table_rows) {
+          err = 1;
+          continue;
+        }
+        const float* c = cos_t + (int64_t)pos[t] * half;
+        const float* s = sin_t + (int64_t)pos[t] * half;
+        for (int64_t i = 0; i < half; i++) {
+          const float x1 = traditional ? x[2 * i] : x[i];
+          const float x2 = traditional ? x[2 * i + 1] : x[i + half];
+          const float re = x1 * c[i] - x2 * s[i];
+          const float im = x1 * s[i] + x2 * c[i];
+          y[traditional ? 2 * i : i] = re;
+          y[traditional ? 2 * i + 1 : i + half] = im;
+        }
+        for (int64_t d = 0; d < D; d++) x[d] = round_to(y[d], dtype);
+      }
+      if (is_q) {
+        for (int64_t d = 0; d < D; d++) store_elem(q_out, (t * Hq + h) * D + d, dtype, x[d]);
+        continue;
+      }
+      if (slots[t] < 0) continue;
+      const int64_t pid = slots[t] / page_size, off = slots[t] % page_size;
+      if (pid >= P) {
+        err = 1;
+        continue;
+      }
+      const int64_t prow = (pid * Hkv + h) * page_size + off;
+      void* pool = is_k ? k_pages : v_pages;
+      if (kv_dtype == OR_I8)
+        quantize_row(x, D, (int8_t*)pool + prow * D, is_k ? k_scales : v_scales, prow, scale_dtype);
+      else
+        for (int64_t d = 0; d < D; d++) store_elem(pool, prow * D + d, kv_dtype, x[d]);
+    }
+  }
+  free(x);
+  free(y);
+  return err;
 }

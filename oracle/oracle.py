@@ -12,6 +12,9 @@ plain Python the pieces of the reference that are Python-level:
 * ``grouped_sdpa_ref``     -- ``attention.py:59-100`` (``causal_mask`` and
   ``scaled_dot_product_attention_grouped``, the reference tests' dense oracle),
 * ``quantize_int8_ref``    -- ``src/nano_vllm_metal/cache/paged.py:152-158``,
+* ``qk_norm_rope_write_ref`` -- ``src/nano_vllm_metal/models/qwen3.py:100-116``
+  (q_norm / k_norm, RoPE of ``layers/rotary_embedding.py:74-124``, the paged write
+  of K and V), with ``rope_tables_ref`` restating ``rotary_embedding.py:28-44``,
 * ``PagePoolRef`` / ``PagedCacheRef`` -- the allocator and append bookkeeping of
   ``paged.py:60-75,197-210,424-459,491-559`` (page ids, page_lens, rewind).
 
@@ -58,6 +61,9 @@ def lib():
         _lib.oracle_paged_attention_int8_decode.argtypes = [P, P, P, P, P, P, P, P, I64, I64, I64, I64, I64, I64, F, I, I]
         _lib.oracle_flash_attention.argtypes = [P, P, P, P, I64, I64, I64, P, I64, I64, I64, I64, I64, I64, F, I, I]
         _lib.oracle_quantize_int8.argtypes = [P, I, I64, I64, P, P]
+        _lib.oracle_qk_norm_rope_write.argtypes = [P, P, P, I, P, P, F, P, P, I64, I, P, P, P, P, I, P, P, I, P,
+                                                   I64, I64, I64, I64, I64, I64]
+        _lib.oracle_qk_norm_rope_write.restype = ctypes.c_int
         _lib.oracle_max_threads.restype = ctypes.c_int
     return _lib
 
@@ -272,6 +278,52 @@ def quantize_int8_ref(x: np.ndarray, in_code: int):
         s = np.empty(x.shape[:-1] + (1,), dtype=np.uint16)
     lib().oracle_quantize_int8(_ptr(x), in_code, rows, D, _ptr(q), _ptr(s))
     return q, s
+
+
+# ---------------------------------------------------------------------------
+# fused q/k norm + RoPE + paged write
+# ---------------------------------------------------------------------------
+
+def rope_tables_ref(dims: int, seq_len: int, base: float = 10000):
+    """rotary_embedding.py:28-44: fp32 cos/sin tables [seq_len, dims // 2]."""
+    half = dims // 2
+    positions = np.arange(seq_len, dtype=np.float32)
+    dim_indices = np.arange(half, dtype=np.float32)
+    inv_freqs = np.power(np.float32(base), -(dim_indices / np.float32(half))).astype(np.float32)
+    freqs = np.outer(positions, inv_freqs).astype(np.float32)
+    return np.cos(freqs).astype(np.float32), np.sin(freqs).astype(np.float32)
+
+
+def qk_norm_rope_write_ref(q, k, v, dtype_code, wq, wk, eps, cos_t, sin_t, traditional, positions,
+                           k_pages, v_pages, kv_code, k_scales, v_scales, scale_code, slots):
+    """qwen3.py:100-116 restated in C (nvm_oracle.c).  q [T, Hq, D], k/v [T, Hkv, D] raw
+    values of dtype_code (uint16 bits for bf16); wq/wk [D] raw or None (RoPE only);
+    cos_t/sin_t fp32 [rows, D/2]; positions int32 [T]; slots int64 [T].  The pools
+    [P, Hkv, page_size, D] (and the int8 scales [P, Hkv, page_size, 1]) are written in
+    place.  Returns (q_out [T, Hq, D] raw, error flag)."""
+    q = np.ascontiguousarray(q)
+    k = np.ascontiguousarray(k)
+    v = np.ascontiguousarray(v)
+    T, Hq, D = q.shape
+    Hkv = k.shape[1]
+    P, _, ps, _ = k_pages.shape
+    for a in (k_pages, v_pages, k_scales, v_scales):
+        if a is not None and not a.flags.c_contiguous:
+            raise ValueError("pools and scales must be C-contiguous (written in place)")
+    cos_t = np.ascontiguousarray(cos_t, dtype=np.float32)
+    sin_t = np.ascontiguousarray(sin_t, dtype=np.float32)
+    pos = np.ascontiguousarray(positions, dtype=np.int32)
+    sl = np.ascontiguousarray(slots, dtype=np.int64)
+    wq_c = None if wq is None else np.ascontiguousarray(wq)
+    wk_c = None if wk is None else np.ascontiguousarray(wk)
+    q_out = np.empty_like(q)
+    err = lib().oracle_qk_norm_rope_write(
+        _ptr(q), _ptr(k), _ptr(v), dtype_code, None if wq_c is None else _ptr(wq_c),
+        None if wk_c is None else _ptr(wk_c), float(eps), _ptr(cos_t), _ptr(sin_t), cos_t.shape[0],
+        1 if traditional else 0, _ptr(pos), _ptr(q_out), _ptr(k_pages), _ptr(v_pages), kv_code,
+        None if k_scales is None else _ptr(k_scales), None if v_scales is None else _ptr(v_scales), scale_code,
+        _ptr(sl), T, Hq, Hkv, D, P, ps)
+    return q_out, int(err)
 
 
 # ---------------------------------------------------------------------------

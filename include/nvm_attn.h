@@ -1,8 +1,9 @@
 /*
  * nvm_attn.h -- C ABI of libnvm_attn.so, the B200 (sm_100a) attention hot path of
  * nano-vllm-metal: paged-attention decode / multi-query, dense flash attention,
- * the paged KV scatter-write (with int8 quantise-on-write) and device-side page
- * allocation for a batch of appends.
+ * the paged KV scatter-write (with int8 quantise-on-write), device-side page
+ * allocation for a batch of appends, and the fused per-layer q/k RMSNorm + RoPE +
+ * K/V write that precedes every attention call.
  *
  * Conventions shared by every entry point
  *   - All tensor arguments are raw DEVICE pointers to row-major contiguous memory
@@ -25,6 +26,8 @@
  *   src/nano_vllm_metal/metal/src/flash_attention.cpp:17-61, 251-352
  *   src/nano_vllm_metal/cache/paged.py:152-195             (page write + int8 quantiser)
  *   src/nano_vllm_metal/cache/paged.py:60-70, 424-459      (page allocation on append)
+ *   src/nano_vllm_metal/models/qwen3.py:100-116            (q/k norm, RoPE, cache update)
+ *   src/nano_vllm_metal/layers/layernorm.py:4-14, layers/rotary_embedding.py:74-124
  */
 #ifndef NVM_ATTN_H_
 #define NVM_ATTN_H_

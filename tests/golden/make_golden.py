@@ -77,6 +77,23 @@ def make_cases():
     x = (rng.standard_normal((3, 2, 16, 128)) * 3).astype(np.float32)
     cases["quant_bf16"] = dict(kind=np.array("quant"), x=o.f32_to_bf16_bits(x), code=np.array(2))
     cases["quant_f16"] = dict(kind=np.array("quant"), x=x.astype(np.float16), code=np.array(1))
+    # fused q/k RMSNorm + RoPE + paged K/V write (Qwen3-0.6B heads 16 / 8, d 128): bf16
+    # pools with halves rotation, and int8 pools (bf16 scales) with the traditional one
+    T, Hq, Hkv, D, P, ps = 6, 16, 8, 128, 3, 4
+    for name, kv_code, trad in [("qkprep_bf16", 2, 0), ("qkprep_i8_trad", 3, 1)]:
+        cos_t, sin_t = o.rope_tables_ref(D, 64, 1000000)
+        slots = rng.permutation(P * ps)[:T].astype(np.int64)
+        slots[2] = -1
+        cases[name] = dict(
+            kind=np.array("qkprep"),
+            q=o.f32_to_bf16_bits((rng.standard_normal((T, Hq, D)) * 4).astype(np.float32)),
+            k=o.f32_to_bf16_bits((rng.standard_normal((T, Hkv, D)) * 2).astype(np.float32)),
+            v=o.f32_to_bf16_bits(rng.standard_normal((T, Hkv, D)).astype(np.float32)),
+            wq=o.f32_to_bf16_bits(rng.uniform(0.5, 1.5, D).astype(np.float32)),
+            wk=o.f32_to_bf16_bits(rng.uniform(0.5, 1.5, D).astype(np.float32)),
+            eps=np.array(1e-6, np.float32), cos=cos_t, sin=sin_t, trad=np.array(trad),
+            pos=rng.integers(0, 64, T).astype(np.int32), slots=slots, kv_code=np.array(kv_code),
+            P=np.array(P), ps=np.array(ps))
     return cases
 
 
@@ -98,6 +115,23 @@ def run_case(o, data: dict) -> dict:
     if kind == "quant":
         q, s = o.quantize_int8_ref(data["x"], int(data["code"]))
         return {"out_q": q, "out_s": s}
+    if kind == "qkprep":
+        T, Hkv, D = data["k"].shape
+        P, ps, kv_code = int(data["P"]), int(data["ps"]), int(data["kv_code"])
+        kp = np.zeros((P, Hkv, ps, D), dtype=np.int8 if kv_code == 3 else np.uint16)
+        vp = np.zeros_like(kp)
+        ks = vs = None
+        if kv_code == 3:
+            ks = np.zeros((P, Hkv, ps, 1), dtype=np.uint16)
+            vs = np.zeros_like(ks)
+        q_out, err = o.qk_norm_rope_write_ref(data["q"], data["k"], data["v"], 2, data["wq"], data["wk"],
+                                              float(data["eps"]), data["cos"], data["sin"], bool(int(data["trad"])),
+                                              data["pos"], kp, vp, kv_code, ks, vs, 2, data["slots"])
+        assert err == 0
+        out = {"out_q": q_out, "out_kp": kp, "out_vp": vp}
+        if kv_code == 3:
+            out.update(out_ks=ks, out_vs=vs)
+        return out
     raise ValueError(kind)
 
 

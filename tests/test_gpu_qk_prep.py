@@ -6,6 +6,8 @@ fp32 RoPE tables.  Shapes follow the Qwen3 models of the reference's benchmarks
 (16/8 heads for 0.6B, 32/8 for 4B, d 128; d 64 as the smaller supported head dim).
 """
 
+import os
+
 import numpy as np
 import pytest
 import torch
@@ -19,6 +21,40 @@ from nano_vllm_b200.layers.rotary_embedding import RoPE
 pytestmark = pytest.mark.gpu
 
 CODE = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2, torch.int8: 3}
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def _bf16(a: np.ndarray, device) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).view(torch.bfloat16).to(device)
+
+
+@pytest.mark.parametrize("name", ["qkprep_bf16", "qkprep_i8_trad"])
+def test_golden_qk_prep(cuda, name):
+    """The committed fixtures (tests/golden/make_golden.py), bit for bit."""
+    d = dict(np.load(os.path.join(GOLDEN, f"{name}.npz")))
+    T, Hq, D = d["q"].shape
+    Hkv = d["k"].shape[1]
+    P, ps, i8 = int(d["P"]), int(d["ps"]), int(d["kv_code"]) == 3
+    rope = RoPE(D, d["cos"].shape[0], 1000000, bool(int(d["trad"])), device=cuda)
+    rope.cos_freqs = torch.from_numpy(d["cos"]).to(cuda)
+    rope.sin_freqs = torch.from_numpy(d["sin"]).to(cuda)
+    kv_dtype = torch.int8 if i8 else torch.bfloat16
+    kp = torch.zeros(P, Hkv, ps, D, dtype=kv_dtype, device=cuda)
+    vp = torch.zeros_like(kp)
+    ks = torch.zeros(P, Hkv, ps, 1, dtype=torch.bfloat16, device=cuda) if i8 else None
+    vs = None if ks is None else torch.zeros_like(ks)
+    out = qk_norm_rope_write(_bf16(d["q"], cuda).reshape(1, T, Hq, D), _bf16(d["k"], cuda).reshape(1, T, Hkv, D),
+                             _bf16(d["v"], cuda).reshape(1, T, Hkv, D), _bf16(d["wq"], cuda), _bf16(d["wk"], cuda),
+                             rope, torch.from_numpy(d["pos"]).to(cuda).reshape(1, T), kp, vp,
+                             torch.from_numpy(d["slots"]).to(cuda), eps=float(d["eps"]), key_scales=ks,
+                             value_scales=vs)
+    assert nv.device_error(cuda) == 0
+    np.testing.assert_array_equal(to_np(out.permute(0, 2, 1, 3).reshape(T, Hq, D)), d["out_q"])
+    np.testing.assert_array_equal(to_np(kp), d["out_kp"])
+    np.testing.assert_array_equal(to_np(vp), d["out_vp"])
+    if i8:
+        np.testing.assert_array_equal(to_np(ks), d["out_ks"])
+        np.testing.assert_array_equal(to_np(vs), d["out_vs"])
 
 
 def _problem(seed, B, L, Hq, Hkv, D, dtype, kv_dtype, P, ps, offsets, skip_every=0):

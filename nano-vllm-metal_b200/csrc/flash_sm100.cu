@@ -987,13 +987,33 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (merge) {
           __threadfence();
           const int64_t base = it.u * p.n_chunks * p.rows_real + row;  // + cc * rows_real
-          float mxc = -INFINITY, lt = 0.f;
+          const int nc = (int)it.n_chunks_unit;
           if (row_ok) {
-            for (int64_t cc = 0; cc < it.n_chunks_unit; ++cc)
-              mxc = fmaxf(mxc, __ldcg(&p.part_ml[base + cc * p.rows_real]).x);
-            for (int64_t cc = 0; cc < it.n_chunks_unit; ++cc) {
-              const float2 ml = __ldcg(&p.part_ml[base + cc * p.rows_real]);
-              if (ml.x != -INFINITY) lt += ml.y * exp2f(ml.x - mxc);
+            // the chunks' (m, l) with one round of loads, then log-sum-exp weights
+            constexpr int kMaxC = 16;
+            float wgt[kMaxC];
+            float mxc = -INFINITY, lt = 0.f;
+            if (nc <= kMaxC) {
+              float2 mlc[kMaxC];
+#pragma unroll
+              for (int cc = 0; cc < kMaxC; ++cc)
+                mlc[cc] = cc < nc ? __ldcg(&p.part_ml[base + cc * p.rows_real]) : make_float2(-INFINITY, 0.f);
+#pragma unroll
+              for (int cc = 0; cc < kMaxC; ++cc) mxc = fmaxf(mxc, mlc[cc].x);
+#pragma unroll
+              for (int cc = 0; cc < kMaxC; ++cc) {
+                wgt[cc] = -1.f;  // chunk without a visible key: skipped
+                if (mlc[cc].x != -INFINITY) {
+                  wgt[cc] = exp2f(mlc[cc].x - mxc);
+                  lt += mlc[cc].y * wgt[cc];
+                }
+              }
+            } else {
+              for (int64_t cc = 0; cc < nc; ++cc) mxc = fmaxf(mxc, __ldcg(&p.part_ml[base + cc * p.rows_real]).x);
+              for (int64_t cc = 0; cc < nc; ++cc) {
+                const float2 ml = __ldcg(&p.part_ml[base + cc * p.rows_real]);
+                if (ml.x != -INFINITY) lt += ml.y * exp2f(ml.x - mxc);
+              }
             }
             const float inv = lt > 0.f ? 1.f / lt : 0.f;
 #pragma unroll 1
@@ -1001,18 +1021,48 @@ __global__ void __launch_bounds__(kThreads, 2)
               float acc2[32];
 #pragma unroll
               for (int x = 0; x < 32; ++x) acc2[x] = 0.f;
-              for (int64_t cc = 0; cc < it.n_chunks_unit; ++cc) {
-                const float2 ml = __ldcg(&p.part_ml[base + cc * p.rows_real]);
-                if (ml.x == -INFINITY) continue;
-                const float w = exp2f(ml.x - mxc);
-                const float4* po = reinterpret_cast<const float4*>(p.part_o + (base + cc * p.rows_real) * kD + c0);
+              if (nc <= kMaxC) {
+                // two chunks' rows in flight per round
+#pragma unroll 1
+                for (int cc = 0; cc < nc; cc += 2) {
+                  float4 o4[2][8];
 #pragma unroll
-                for (int x = 0; x < 8; ++x) {
-                  const float4 o4 = __ldcg(po + x);
-                  acc2[4 * x] += w * o4.x;
-                  acc2[4 * x + 1] += w * o4.y;
-                  acc2[4 * x + 2] += w * o4.z;
-                  acc2[4 * x + 3] += w * o4.w;
+                  for (int j = 0; j < 2; ++j) {
+                    const float4* po = reinterpret_cast<const float4*>(p.part_o + (base + (cc + j) * p.rows_real) * kD + c0);
+#pragma unroll
+                    for (int x = 0; x < 8; ++x) o4[j][x] = cc + j < nc ? __ldcg(po + x) : make_float4(0.f, 0.f, 0.f, 0.f);
+                  }
+#pragma unroll
+                  for (int j = 0; j < 2; ++j) {
+                    float w = -1.f;
+#pragma unroll
+                    for (int q = 0; q < kMaxC; ++q)
+                      if (q == cc + j) w = wgt[q];
+                    if (cc + j < nc && w >= 0.f) {
+#pragma unroll
+                      for (int x = 0; x < 8; ++x) {
+                        acc2[4 * x] += w * o4[j][x].x;
+                        acc2[4 * x + 1] += w * o4[j][x].y;
+                        acc2[4 * x + 2] += w * o4[j][x].z;
+                        acc2[4 * x + 3] += w * o4[j][x].w;
+                      }
+                    }
+                  }
+                }
+              } else {
+                for (int64_t cc = 0; cc < nc; ++cc) {
+                  const float2 ml = __ldcg(&p.part_ml[base + cc * p.rows_real]);
+                  if (ml.x == -INFINITY) continue;
+                  const float w = exp2f(ml.x - mxc);
+                  const float4* po = reinterpret_cast<const float4*>(p.part_o + (base + cc * p.rows_real) * kD + c0);
+#pragma unroll
+                  for (int x = 0; x < 8; ++x) {
+                    const float4 o4 = __ldcg(po + x);
+                    acc2[4 * x] += w * o4.x;
+                    acc2[4 * x + 1] += w * o4.y;
+                    acc2[4 * x + 2] += w * o4.z;
+                    acc2[4 * x + 3] += w * o4.w;
+                  }
                 }
               }
               if (p.stage_out) stage32(acc2, c0, inv);

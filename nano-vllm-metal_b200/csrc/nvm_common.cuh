@@ -62,6 +62,22 @@ __device__ __forceinline__ float load_dyn(const void* p, int64_t i, int dtype) {
   }
 }
 
+// Elements i and i + 1 (i even, the pointer aligned to two elements) as one load.
+template <typename T>
+__device__ __forceinline__ float2 load_pair(const void* p, int64_t i);
+template <>
+__device__ __forceinline__ float2 load_pair<float>(const void* p, int64_t i) {
+  return __ldg(reinterpret_cast<const float2*>(p) + (i >> 1));
+}
+template <>
+__device__ __forceinline__ float2 load_pair<__half>(const void* p, int64_t i) {
+  return __half22float2(__ldg(reinterpret_cast<const __half2*>(p) + (i >> 1)));
+}
+template <>
+__device__ __forceinline__ float2 load_pair<__nv_bfloat16>(const void* p, int64_t i) {
+  return __bfloat1622float2(__ldg(reinterpret_cast<const __nv_bfloat162*>(p) + (i >> 1)));
+}
+
 __device__ __forceinline__ void store_dyn(void* p, int64_t i, int dtype, float v) {
   switch (dtype) {
     case NVM_F32: reinterpret_cast<float*>(p)[i] = v; break;

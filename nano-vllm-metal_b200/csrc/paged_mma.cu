@@ -151,6 +151,49 @@ __global__ void __launch_bounds__(Cfg<KvT, D, NWM, NWK, NS_>::kThreads)
     }
     fence_mbar_init();
   }
+  // Consumers load their Q fragments while the producer reads the block table: one
+  // round of independent vector loads (pairs of elements), dtype dispatch outside.
+  const int wm = warp % NWM, wk = warp / NWM;
+  const int r = lane >> 2, cq = lane & 3;
+  const int64_t q_row0 = (b * p.Hq + h * p.g) * p.L;  // flat row of (b, h, m = 0)
+  const int64_t mA = row0 + wm * 16 + r, mB = mA + 8;  // this thread's two rows (unit-relative)
+  const bool vA = mA < p.M, vB = mB < p.M;
+  uint32_t qa[NKS][4];
+  if (warp < C::kCons) {
+    const int64_t offA = (q_row0 + mA) * D, offB = (q_row0 + mB) * D;
+    auto load_q = [&](auto tag) {
+      using QT = decltype(tag);
+      float2 va[NKS][2], vb[NKS][2];
+#pragma unroll
+      for (int ks = 0; ks < NKS; ++ks) {
+        int d0, d1;  // first d of the low / high k pair of this thread in k-step ks
+        if (C::kI8) {
+          d0 = 32 * cq + 4 * ks;
+          d1 = d0 + 2;
+        } else {
+          d0 = 16 * ks + 2 * cq;
+          d1 = d0 + 8;
+        }
+        va[ks][0] = vA ? load_pair<QT>(p.q, offA + d0) : make_float2(0.f, 0.f);
+        va[ks][1] = vA ? load_pair<QT>(p.q, offA + d1) : make_float2(0.f, 0.f);
+        vb[ks][0] = vB ? load_pair<QT>(p.q, offB + d0) : make_float2(0.f, 0.f);
+        vb[ks][1] = vB ? load_pair<QT>(p.q, offB + d1) : make_float2(0.f, 0.f);
+      }
+#pragma unroll
+      for (int ks = 0; ks < NKS; ++ks) {
+        qa[ks][0] = pack2<MmaT>(va[ks][0].x, va[ks][0].y);
+        qa[ks][1] = pack2<MmaT>(vb[ks][0].x, vb[ks][0].y);
+        qa[ks][2] = pack2<MmaT>(va[ks][1].x, va[ks][1].y);
+        qa[ks][3] = pack2<MmaT>(vb[ks][1].x, vb[ks][1].y);
+      }
+    };
+    if (p.q_dtype == NVM_F32)
+      load_q(float{});
+    else if (p.q_dtype == NVM_F16)
+      load_q(__half{});
+    else
+      load_q(__nv_bfloat16{});
+  }
   if (warp == C::kCons) {
     for (int i = lane; i < n_my; i += 32) {
       const int64_t tok0 = (t_begin + i) * 16;
@@ -207,35 +250,7 @@ __global__ void __launch_bounds__(Cfg<KvT, D, NWM, NWK, NS_>::kThreads)
   }
 
   // ------------------------------------------------------------------ consumers
-  const int wm = warp % NWM, wk = warp / NWM;
-  const int r = lane >> 2, cq = lane & 3;
-  const int64_t q_row0 = (b * p.Hq + h * p.g) * p.L;  // flat row of (b, h, m = 0)
-  const int64_t mA = row0 + wm * 16 + r, mB = mA + 8;  // this thread's two rows (unit-relative)
-  const bool vA = mA < p.M, vB = mB < p.M;
 
-  uint32_t qa[NKS][4];
-  {
-    const int64_t offA = (q_row0 + mA) * D, offB = (q_row0 + mB) * D;
-#pragma unroll
-    for (int ks = 0; ks < NKS; ++ks) {
-      int d0, d1;  // first d of the low / high k pair of this thread in k-step ks
-      if (C::kI8) {
-        d0 = 32 * cq + 4 * ks;
-        d1 = d0 + 2;
-      } else {
-        d0 = 16 * ks + 2 * cq;
-        d1 = d0 + 8;
-      }
-      float a0 = vA ? load_dyn(p.q, offA + d0, p.q_dtype) : 0.f, a1 = vA ? load_dyn(p.q, offA + d0 + 1, p.q_dtype) : 0.f;
-      float b0 = vB ? load_dyn(p.q, offB + d0, p.q_dtype) : 0.f, b1 = vB ? load_dyn(p.q, offB + d0 + 1, p.q_dtype) : 0.f;
-      float a2 = vA ? load_dyn(p.q, offA + d1, p.q_dtype) : 0.f, a3 = vA ? load_dyn(p.q, offA + d1 + 1, p.q_dtype) : 0.f;
-      float b2 = vB ? load_dyn(p.q, offB + d1, p.q_dtype) : 0.f, b3 = vB ? load_dyn(p.q, offB + d1 + 1, p.q_dtype) : 0.f;
-      qa[ks][0] = pack2<MmaT>(a0, a1);
-      qa[ks][1] = pack2<MmaT>(b0, b1);
-      qa[ks][2] = pack2<MmaT>(a2, a3);
-      qa[ks][3] = pack2<MmaT>(b2, b3);
-    }
-  }
   // Inclusive last visible key of each row (rows past M never mask anything).
   const int64_t BIG = INT64_MAX / 4;
   int64_t limA = BIG, limB = BIG;
@@ -501,6 +516,69 @@ __global__ void __launch_bounds__(Cfg<KvT, D, NWM, NWK, NS_>::kThreads)
   if (!*s_flag) return;
   __threadfence();
   const int64_t base = unit * p.n_chunks * p.rows_real;
+  if ((2 * n_chunks + 1) * rows_here * (int64_t)sizeof(float) <= C::kMainBytes) {
+    // Stage every chunk's (m, l) in shared memory with one parallel round of loads, turn
+    // them into the log-sum-exp weights f = 2^(m_c - max m) (-1 marks a chunk without
+    // keys), then sum the partial O rows with all chunk loads independent of one another.
+    // Same operations in the same chunk order as the one-thread-per-element loop below.
+    float* wm = reinterpret_cast<float*>(smem);  // [n_chunks][rows_here]: m, then the weight f
+    float* wlc = wm + n_chunks * rows_here;      // [n_chunks][rows_here]: l
+    float* wl = wlc + n_chunks * rows_here;      // [rows_here]: sum of l * f
+    for (int64_t i = tid; i < n_chunks * rows_here; i += NCT) {
+      const int64_t cc = i / rows_here, rl = i % rows_here;
+      const float2 ml = __ldcg(&p.part_ml[base + cc * p.rows_real + rl]);
+      wm[i] = ml.x;
+      wlc[i] = ml.y;
+    }
+    named_barrier(1, NCT);
+    for (int64_t rl = tid; rl < rows_here; rl += NCT) {
+      float ms = -INFINITY;
+      for (int64_t cc = 0; cc < n_chunks; ++cc) ms = fmaxf(ms, wm[cc * rows_here + rl]);
+      float ls = 0.f;
+      for (int64_t cc = 0; cc < n_chunks; ++cc) {
+        const float mc = wm[cc * rows_here + rl];
+        float f = -1.f;
+        if (mc != -INFINITY) {
+          f = exp2f(mc - ms);
+          ls += wlc[cc * rows_here + rl] * f;
+        }
+        wm[cc * rows_here + rl] = f;
+      }
+      wl[rl] = ls;
+    }
+    named_barrier(1, NCT);
+    // four consecutive d per thread (16-byte loads), eight chunks' loads in flight at once
+    const int64_t cstride = p.rows_real * D;
+    for (int64_t g4 = tid; g4 < rows_here * (D / 4); g4 += NCT) {
+      const int rl = (int)(g4 / (D / 4)), d = (int)(g4 % (D / 4)) * 4;
+      const float* po = p.part_o + (base + rl) * D + d;
+      float os[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int64_t cc = 0; cc < n_chunks; cc += 8) {
+        float4 v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          v[j] = cc + j < n_chunks ? __ldcg(reinterpret_cast<const float4*>(po + (cc + j) * cstride))
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (cc + j >= n_chunks) break;
+          const float f = wm[(cc + j) * rows_here + rl];
+          if (f >= 0.f) {
+            os[0] += v[j].x * f;
+            os[1] += v[j].y * f;
+            os[2] += v[j].z * f;
+            os[3] += v[j].w * f;
+          }
+        }
+      }
+      const float ls = wl[rl];
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        store_dyn(p.out, (q_row0 + row0 + rl) * D + d + e, p.out_dtype, ls > 0.f ? os[e] / ls : 0.f);
+    }
+    if (tid == 0) p.counters[unit] = 0;
+    return;
+  }
   for (int64_t idx = tid; idx < rows_here * D; idx += NCT) {
     const int rl = (int)(idx / D), d = (int)(idx % D);
     float ms = -INFINITY;
@@ -650,6 +728,8 @@ MmaPlan plan_paged_mma(const PagedArgs& a) {
   if (a.max_pages <= 0) return plan;
   auto al16 = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
   if (!al16(a.k_pages) || !al16(a.v_pages)) return plan;
+  // q is read as element pairs
+  if ((reinterpret_cast<uintptr_t>(a.q) & (a.q_dtype == NVM_F32 ? 7 : 3)) != 0) return plan;
   if (kv8 && (!al16(a.k_scales) || !al16(a.v_scales))) return plan;
   const int64_t M = (a.Hq / a.Hkv) * a.L;
   plan.nwm = M <= 16 ? 1 : (M <= 32 ? 2 : (M <= 48 ? 3 : 4));

@@ -85,6 +85,12 @@ struct Cfg {
   static_assert(!kI8 || D == 128, "int8 path needs D == 128");
 };
 
+__device__ __forceinline__ float ex2_ftz(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // bf16 pair of the rounding residuals (a - hi.x, b - hi.y) of a packed bf16 pair.
 __device__ __forceinline__ uint32_t pack_residual(float a, float b, uint32_t hi) {
   const __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&hi);
@@ -365,24 +371,30 @@ __global__ void __launch_bounds__(Cfg<KvT, D, NWM, NWK, NS_>::kThreads)
       mxB = fmaxf(mxB, __shfl_xor_sync(0xffffffffu, mxB, 2));
       const float mnA = fmaxf(mrA, mxA), mnB = fmaxf(mrB, mxB);
       const float muA = mnA == -INFINITY ? 0.f : mnA, muB = mnB == -INFINITY ? 0.f : mnB;
-      const float alA = exp2f(mrA - muA), alB = exp2f(mrB - muB);
+      // 2^x on the MUFU unit (ex2.approx.ftz: 2 ulp, -inf -> +0)
+      const float alA = ex2_ftz(mrA - muA), alB = ex2_ftz(mrB - muB);
+      const bool moved = mrA != mnA || mrB != mnB;  // a row max changed: O needs rescaling
       mrA = mnA;
       mrB = mnB;
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt) {
-        sc[nt][0] = exp2f(sc[nt][0] - muA);
-        sc[nt][1] = exp2f(sc[nt][1] - muA);
-        sc[nt][2] = exp2f(sc[nt][2] - muB);
-        sc[nt][3] = exp2f(sc[nt][3] - muB);
+        sc[nt][0] = ex2_ftz(sc[nt][0] - muA);
+        sc[nt][1] = ex2_ftz(sc[nt][1] - muA);
+        sc[nt][2] = ex2_ftz(sc[nt][2] - muB);
+        sc[nt][3] = ex2_ftz(sc[nt][3] - muB);
       }
       lA = lA * alA + (sc[0][0] + sc[0][1] + sc[1][0] + sc[1][1]);
       lB = lB * alB + (sc[0][2] + sc[0][3] + sc[1][2] + sc[1][3]);
+      // alpha is exactly 1 for rows whose max did not move (and for rows without a key
+      // yet, whose O is 0): skipping the multiply then changes nothing
+      if (__any_sync(0xffffffffu, moved)) {
 #pragma unroll
-      for (int i2 = 0; i2 < NDT; ++i2) {
-        o[i2][0] *= alA;
-        o[i2][1] *= alA;
-        o[i2][2] *= alB;
-        o[i2][3] *= alB;
+        for (int i2 = 0; i2 < NDT; ++i2) {
+          o[i2][0] *= alA;
+          o[i2][1] *= alA;
+          o[i2][2] *= alB;
+          o[i2][3] *= alB;
+        }
       }
       uint32_t pa[4], pl[4];
       pa[0] = pack2<MmaT>(sc[0][0], sc[0][1]);

@@ -66,9 +66,13 @@ struct Cfg {
   static constexpr bool kI8 = std::is_same<KvT, int8_t>::value;
   using MmaT = typename std::conditional<kI8, __half, KvT>::type;
   static constexpr bool kSplitP = std::is_same<KvT, __nv_bfloat16>::value;
-  static constexpr int kCons = NWM * NWK;
+  // NWM == 0 selects the n8 tile: keys are the mma's M (16 per tile) and up to eight
+  // query rows its N, so S^T = K Q^T and O^T = V^T P^T take half the mma.sync of the
+  // 16-row tile when a kv head has at most eight query rows.
+  static constexpr bool kN8 = NWM == 0;
+  static constexpr int kCons = (kN8 ? 1 : NWM) * NWK;
   static constexpr int kThreads = (kCons + 1) * 32;
-  static constexpr int kRB = 16 * NWM;
+  static constexpr int kRB = kN8 ? 8 : 16 * NWM;
   static constexpr int kTileBytes = 16 * D * (int)sizeof(KvT);
   // K scales at +0, V scales at +128 past the two tiles: TMA destinations are 128-byte aligned.
   static constexpr int kScaleBytes = kI8 ? 256 : 0;
@@ -84,6 +88,14 @@ struct Cfg {
   static_assert(D % 64 == 0, "head dim must be 64 or 128");
   static_assert(!kI8 || D == 128, "int8 path needs D == 128");
 };
+
+// 8x8 b16 matrix held in the mma accumulator layout (row lane/4, columns 2(lane%4), +1),
+// transposed across the warp (PTX movmatrix)
+__device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
 
 __device__ __forceinline__ float ex2_ftz(float x) {
   float y;
@@ -153,17 +165,21 @@ __global__ void __launch_bounds__(Cfg<KvT, D, NWM, NWK, NS_>::kThreads)
   if (threadIdx.x == 0) {
     for (int s = 0; s < NS; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], NWM);
+      mbar_init(&empty[s], C::kN8 ? 1 : NWM);
     }
     fence_mbar_init();
   }
   // Consumers load their Q fragments while the producer reads the block table: one
   // round of independent vector loads (pairs of elements), dtype dispatch outside.
-  const int wm = warp % NWM, wk = warp / NWM;
+  constexpr int kWM = C::kN8 ? 1 : NWM;
+  const int wm = warp % kWM, wk = warp / kWM;
   const int r = lane >> 2, cq = lane & 3;
   const int64_t q_row0 = (b * p.Hq + h * p.g) * p.L;  // flat row of (b, h, m = 0)
-  const int64_t mA = row0 + wm * 16 + r, mB = mA + 8;  // this thread's two rows (unit-relative)
+  // this thread's two softmax rows (unit-relative): m16 tile rows r, r + 8; n8 tile
+  // columns 2 cq, 2 cq + 1.  The n8 tile's Q operand is row r (loaded as "row A").
+  const int64_t mA = C::kN8 ? row0 + r : row0 + wm * 16 + r, mB = C::kN8 ? p.M : mA + 8;
   const bool vA = mA < p.M, vB = mB < p.M;
+  const int64_t sA = C::kN8 ? row0 + 2 * cq : mA, sB = C::kN8 ? sA + 1 : mB;
   uint32_t qa[NKS][4];
   if (warp < C::kCons) {
     const int64_t offA = (q_row0 + mA) * D, offB = (q_row0 + mB) * D;
@@ -261,8 +277,8 @@ __global__ void __launch_bounds__(Cfg<KvT, D, NWM, NWK, NS_>::kThreads)
   const int64_t BIG = INT64_MAX / 4;
   int64_t limA = BIG, limB = BIG;
   if (p.causal) {
-    if (vA) limA = (mA % p.L) + ctx - p.L;
-    if (vB) limB = (mB % p.L) + ctx - p.L;
+    if (sA < p.M) limA = (sA % p.L) + ctx - p.L;
+    if (sB < p.M) limB = (sB % p.L) + ctx - p.L;
   }
   // Keys below `clean` are visible to every real row of this warp: no masking there.
   int64_t clean = ctx_limit;
@@ -291,6 +307,152 @@ __global__ void __launch_bounds__(Cfg<KvT, D, NWM, NWK, NS_>::kThreads)
       break;
     }
     if (stage_valid[s]) {
+      if constexpr (C::kN8) {
+      const int64_t tok0 = (t_begin + i) * 16;
+      const uint32_t kt = smem_u32(smem + s * C::kStageBytes);
+      const uint32_t vt = kt + C::kTileBytes;
+      // S^T = K Q^T (16 keys x 8 rows); even / odd k-steps in two accumulator chains
+      float sacc[2][4];
+#pragma unroll
+      for (int q2 = 0; q2 < 2; ++q2) sacc[q2][0] = sacc[q2][1] = sacc[q2][2] = sacc[q2][3] = 0.f;
+      if constexpr (!C::kI8) {
+        const int mi = lane >> 3;
+        const int ktok = (mi >> 1) * 8 + (lane & 7);
+#pragma unroll
+        for (int ks = 0; ks < NKS; ++ks) {
+          uint32_t k0, k1, k2, k3;
+          ldsm_x4(swz(kt, ktok, 2 * ks + (mi & 1)), k0, k1, k2, k3);
+          const uint32_t a[4] = {k0, k2, k1, k3};
+          mma16816<MmaT>(sacc[ks & 1], a, qa[ks][0], qa[ks][2]);
+        }
+      } else {
+        // keys r and r + 8, bytes [32 cq, 32 cq + 32) of each (the k dimension is
+        // permuted identically in Q: k pair (2cq, 2cq+1) <-> d 32cq + 4ks + {0,1},
+        // k pair (2cq+8, 2cq+9) <-> d 32cq + 4ks + {2,3})
+        uint32_t kw[2][8];
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          const int tok = hf * 8 + r;
+          lds128(swz(kt, tok, 2 * cq), kw[hf][0], kw[hf][1], kw[hf][2], kw[hf][3]);
+          lds128(swz(kt, tok, 2 * cq + 1), kw[hf][4], kw[hf][5], kw[hf][6], kw[hf][7]);
+        }
+#pragma unroll
+        for (int ks = 0; ks < NKS; ++ks) {
+          const uint32_t x0 = kw[0][ks] ^ 0x80808080u, x1 = kw[1][ks] ^ 0x80808080u;
+          const uint32_t a[4] = {i8pair_to_f16x2(x0, 0x4140u), i8pair_to_f16x2(x1, 0x4140u),
+                                 i8pair_to_f16x2(x0, 0x4342u), i8pair_to_f16x2(x1, 0x4342u)};
+          mma16816<MmaT>(sacc[ks & 1], a, qa[ks][0], qa[ks][2]);
+        }
+        const ScaleT* ksp = reinterpret_cast<const ScaleT*>(smem + s * C::kStageBytes + 2 * C::kTileBytes);
+        const float k0 = to_f32(ksp[r]), k1 = to_f32(ksp[r + 8]);
+        sacc[0][0] *= k0;
+        sacc[0][1] *= k0;
+        sacc[0][2] *= k1;
+        sacc[0][3] *= k1;
+        sacc[1][0] *= k0;
+        sacc[1][1] *= k0;
+        sacc[1][2] *= k1;
+        sacc[1][3] *= k1;
+      }
+      // sv[0] = (key r, row 2cq), [1] = (key r, row 2cq+1), [2] = (key r+8, row 2cq), [3] = (key r+8, row 2cq+1)
+      float sv[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sv[e] = sacc[0][e] + sacc[1][e];
+      const bool need_mask = tok0 + 16 > clean;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float v = sv[e] * p.scale_log2;
+        if (need_mask) {
+          const int64_t tok = tok0 + r + 8 * (e >> 1);
+          const int64_t lim = (e & 1) ? limB : limA;
+          if (tok >= ctx_limit || tok > lim) v = -INFINITY;
+        }
+        sv[e] = v;
+      }
+      // row max over the 16 keys: two in the thread, the rest across r (lanes xor 4, 8, 16)
+      float mxA = fmaxf(sv[0], sv[2]), mxB = fmaxf(sv[1], sv[3]);
+#pragma unroll
+      for (int o2 = 4; o2 < 32; o2 <<= 1) {
+        mxA = fmaxf(mxA, __shfl_xor_sync(0xffffffffu, mxA, o2));
+        mxB = fmaxf(mxB, __shfl_xor_sync(0xffffffffu, mxB, o2));
+      }
+      const float mnA = fmaxf(mrA, mxA), mnB = fmaxf(mrB, mxB);
+      const float muA = mnA == -INFINITY ? 0.f : mnA, muB = mnB == -INFINITY ? 0.f : mnB;
+      const float alA = ex2_ftz(mrA - muA), alB = ex2_ftz(mrB - muB);
+      const bool moved = mrA != mnA || mrB != mnB;
+      mrA = mnA;
+      mrB = mnB;
+      sv[0] = ex2_ftz(sv[0] - muA);
+      sv[1] = ex2_ftz(sv[1] - muB);
+      sv[2] = ex2_ftz(sv[2] - muA);
+      sv[3] = ex2_ftz(sv[3] - muB);
+      lA = lA * alA + (sv[0] + sv[2]);
+      lB = lB * alB + (sv[1] + sv[3]);
+      if (__any_sync(0xffffffffu, moved)) {
+#pragma unroll
+        for (int j = 0; j < D / 16; ++j) {
+          o[j][0] *= alA;
+          o[j][1] *= alB;
+          o[j][2] *= alA;
+          o[j][3] *= alB;
+        }
+      }
+      // P^T as the B operand (keys x rows): each 8 x 8 quadrant of P^T's accumulator
+      // layout transposed in registers
+      uint32_t pb[2], pbl[2];
+      pb[0] = movmatrix_t(pack2<MmaT>(sv[0], sv[1]));
+      pb[1] = movmatrix_t(pack2<MmaT>(sv[2], sv[3]));
+      if constexpr (C::kSplitP) {
+        const uint32_t h0 = pack2<MmaT>(sv[0], sv[1]), h1 = pack2<MmaT>(sv[2], sv[3]);
+        pbl[0] = movmatrix_t(pack_residual(sv[0], sv[1], h0));
+        pbl[1] = movmatrix_t(pack_residual(sv[2], sv[3], h1));
+      }
+      // O^T += V^T P^T, one m16 tile of d per mma
+      if constexpr (!C::kI8) {
+        const int mi = lane >> 3;
+        const int vtok = (mi & 1) * 8 + (lane & 7);
+#pragma unroll
+        for (int j = 0; j < D / 16; ++j) {
+          uint32_t v0, v1, v2, v3;
+          ldsm_x4_t(swz(vt, vtok, 2 * j + (mi >> 1)), v0, v1, v2, v3);
+          const uint32_t a[4] = {v0, v2, v1, v3};
+          mma16816<MmaT>(o[j], a, pb[0], pb[1]);
+          if constexpr (C::kSplitP) mma16816<MmaT>(o[j], a, pbl[0], pbl[1]);
+        }
+      } else {
+        // V rows 2cq, 2cq+1, 2cq+8, 2cq+9, bytes [16 r, 16 r + 16): tile j row r <-> d 16r + 2j,
+        // row r + 8 <-> d 16r + 2j + 1
+        uint32_t vw[4][4];
+#pragma unroll
+        for (int t4 = 0; t4 < 4; ++t4) {
+          const int tok = 2 * cq + (t4 & 1) + (t4 >> 1) * 8;
+          lds128(swz(vt, tok, r), vw[t4][0], vw[t4][1], vw[t4][2], vw[t4][3]);
+        }
+        const ScaleT* vsp = reinterpret_cast<const ScaleT*>(smem + s * C::kStageBytes + 2 * C::kTileBytes + 128);
+        const __half2 vlo = __floats2half2_rn(to_f32(vsp[2 * cq]), to_f32(vsp[2 * cq + 1]));
+        const __half2 vhi = __floats2half2_rn(to_f32(vsp[2 * cq + 8]), to_f32(vsp[2 * cq + 9]));
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+          const uint32_t y01 = prmt(vw[0][w], vw[1][w], 0x5140u) ^ 0x80808080u;
+          const uint32_t y23 = prmt(vw[0][w], vw[1][w], 0x7362u) ^ 0x80808080u;
+          const uint32_t z01 = prmt(vw[2][w], vw[3][w], 0x5140u) ^ 0x80808080u;
+          const uint32_t z23 = prmt(vw[2][w], vw[3][w], 0x7362u) ^ 0x80808080u;
+#pragma unroll
+          for (int jj = 0; jj < 2; ++jj) {
+            const uint32_t y = jj ? y23 : y01, z = jj ? z23 : z01;
+            uint32_t e0 = i8pair_to_f16x2(y, 0x4140u), e1 = i8pair_to_f16x2(y, 0x4342u);
+            uint32_t e2 = i8pair_to_f16x2(z, 0x4140u), e3 = i8pair_to_f16x2(z, 0x4342u);
+            __half2 f0 = __hmul2(*reinterpret_cast<__half2*>(&e0), vlo);
+            __half2 f1 = __hmul2(*reinterpret_cast<__half2*>(&e1), vlo);
+            __half2 f2 = __hmul2(*reinterpret_cast<__half2*>(&e2), vhi);
+            __half2 f3 = __hmul2(*reinterpret_cast<__half2*>(&e3), vhi);
+            const uint32_t a[4] = {*reinterpret_cast<uint32_t*>(&f0), *reinterpret_cast<uint32_t*>(&f1),
+                                   *reinterpret_cast<uint32_t*>(&f2), *reinterpret_cast<uint32_t*>(&f3)};
+            mma16816<MmaT>(o[2 * w + jj], a, pb[0], pb[1]);
+          }
+        }
+      }
+      } else {
       const int64_t tok0 = (t_begin + i) * 16;
       const uint32_t kt = smem_u32(smem + s * C::kStageBytes);
       const uint32_t vt = kt + C::kTileBytes;
@@ -452,6 +614,7 @@ __global__ void __launch_bounds__(Cfg<KvT, D, NWM, NWK, NS_>::kThreads)
           }
         }
       }
+          }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[(i % NS)]);
@@ -460,10 +623,19 @@ __global__ void __launch_bounds__(Cfg<KvT, D, NWM, NWK, NS_>::kThreads)
   // warp waits forever); its rows carry garbage and the error word is set.
   (void)timed_out;
 
-  lA += __shfl_xor_sync(0xffffffffu, lA, 1);
-  lA += __shfl_xor_sync(0xffffffffu, lA, 2);
-  lB += __shfl_xor_sync(0xffffffffu, lB, 1);
-  lB += __shfl_xor_sync(0xffffffffu, lB, 2);
+  if constexpr (C::kN8) {
+    // row sums: partial over this thread's keys, reduced across r
+#pragma unroll
+    for (int o2 = 4; o2 < 32; o2 <<= 1) {
+      lA += __shfl_xor_sync(0xffffffffu, lA, o2);
+      lB += __shfl_xor_sync(0xffffffffu, lB, o2);
+    }
+  } else {
+    lA += __shfl_xor_sync(0xffffffffu, lA, 1);
+    lA += __shfl_xor_sync(0xffffffffu, lA, 2);
+    lB += __shfl_xor_sync(0xffffffffu, lB, 1);
+    lB += __shfl_xor_sync(0xffffffffu, lB, 2);
+  }
 
   // ------------------------------------------------------------------ epilogue
   constexpr int NCT = C::kCons * 32;
@@ -471,7 +643,24 @@ __global__ void __launch_bounds__(Cfg<KvT, D, NWM, NWK, NS_>::kThreads)
   float* eo = reinterpret_cast<float*>(smem);  // [NWK][RB][D]
   float* em = eo + NWK * C::kRB * D;            // [NWK][RB]
   float* el = em + NWK * C::kRB;                // [NWK][RB]
-  {
+  if constexpr (C::kN8) {
+    const int rlA = 2 * cq, rlB = rlA + 1;
+#pragma unroll
+    for (int j = 0; j < D / 16; ++j) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int d = C::kI8 ? 16 * r + 2 * j + (e >> 1) : 16 * j + 8 * (e >> 1) + r;
+        const int rl = (e & 1) ? rlB : rlA;
+        eo[(wk * C::kRB + rl) * D + d] = o[j][e];
+      }
+    }
+    if (r == 0) {
+      em[wk * C::kRB + rlA] = mrA;
+      el[wk * C::kRB + rlA] = lA;
+      em[wk * C::kRB + rlB] = mrB;
+      el[wk * C::kRB + rlB] = lB;
+    }
+  } else {
     const int rlA = wm * 16 + r, rlB = rlA + 8;
 #pragma unroll
     for (int nd = 0; nd < NDT; ++nd) {
@@ -690,17 +879,17 @@ int launch_cfg(const PagedArgs& a, const MmaPlan& plan, void* ws, cudaStream_t s
 // 16-bit decode reached 98% of measured HBM bandwidth with 2 consumer warps and 6
 // stages (4 CTAs per SM) against 64% with 4 warps and 8 stages (2 CTAs per SM).
 // NVM_ATTN_DECODE_CFG selects another variant (for sweeps).
-template <typename KvT, typename ScaleT, int D>
+template <typename KvT, typename ScaleT, int D, int NWM>
 int launch_decode(const PagedArgs& a, const MmaPlan& plan, void* ws, cudaStream_t s) {
   switch (plan.variant) {
-    case 0: return launch_cfg<KvT, ScaleT, D, 1, 4>(a, plan, ws, s);
-    case 1: return launch_cfg<KvT, ScaleT, D, 1, 4, 12>(a, plan, ws, s);
-    case 3: return launch_cfg<KvT, ScaleT, D, 1, 2, 6>(a, plan, ws, s);
-    case 4: return launch_cfg<KvT, ScaleT, D, 1, 2, 8>(a, plan, ws, s);
-    case 6: return launch_cfg<KvT, ScaleT, D, 1, 1, 4>(a, plan, ws, s);
-    case 7: return launch_cfg<KvT, ScaleT, D, 1, 2, 4>(a, plan, ws, s);
-    case 8: return launch_cfg<KvT, ScaleT, D, 1, 1, 6>(a, plan, ws, s);
-    default: return launch_cfg<KvT, ScaleT, D, 1, 2, 6>(a, plan, ws, s);
+    case 0: return launch_cfg<KvT, ScaleT, D, NWM, 4>(a, plan, ws, s);
+    case 1: return launch_cfg<KvT, ScaleT, D, NWM, 4, 12>(a, plan, ws, s);
+    case 3: return launch_cfg<KvT, ScaleT, D, NWM, 2, 6>(a, plan, ws, s);
+    case 4: return launch_cfg<KvT, ScaleT, D, NWM, 2, 8>(a, plan, ws, s);
+    case 6: return launch_cfg<KvT, ScaleT, D, NWM, 1, 4>(a, plan, ws, s);
+    case 7: return launch_cfg<KvT, ScaleT, D, NWM, 2, 4>(a, plan, ws, s);
+    case 8: return launch_cfg<KvT, ScaleT, D, NWM, 1, 6>(a, plan, ws, s);
+    default: return launch_cfg<KvT, ScaleT, D, NWM, 2, 6>(a, plan, ws, s);
   }
 }
 
@@ -719,7 +908,8 @@ int launch_m3(const PagedArgs& a, const MmaPlan& plan, void* ws, cudaStream_t s)
 template <typename KvT, typename ScaleT, int D>
 int launch_d(const PagedArgs& a, const MmaPlan& plan, void* ws, cudaStream_t s) {
   switch (plan.nwm) {
-    case 1: return launch_decode<KvT, ScaleT, D>(a, plan, ws, s);
+    case 0: return launch_decode<KvT, ScaleT, D, 0>(a, plan, ws, s);
+    case 1: return launch_decode<KvT, ScaleT, D, 1>(a, plan, ws, s);
     case 2: return launch_cfg<KvT, ScaleT, D, 2, 2>(a, plan, ws, s);
     case 3: return launch_m3<KvT, ScaleT, D>(a, plan, ws, s);
     default: return launch_cfg<KvT, ScaleT, D, 4, 1>(a, plan, ws, s);
@@ -745,10 +935,12 @@ MmaPlan plan_paged_mma(const PagedArgs& a) {
   if (kv8 && (!al16(a.k_scales) || !al16(a.v_scales))) return plan;
   const int64_t M = (a.Hq / a.Hkv) * a.L;
   plan.nwm = M <= 16 ? 1 : (M <= 32 ? 2 : (M <= 48 ? 3 : 4));
-  plan.nwk = plan.nwm == 1 ? 4 : (plan.nwm == 4 ? 1 : 2);
+  // at most eight query rows per kv head: the n8 tile (nwm = 0)
+  if (M <= 8 && env_int("NVM_ATTN_N8", 1) != 0) plan.nwm = 0;
+  plan.nwk = plan.nwm <= 1 ? 4 : (plan.nwm == 4 ? 1 : 2);
   // variant -> consumer warps along keys (must match launch_decode / launch_m3)
   plan.variant = -1;
-  if (plan.nwm == 1) {
+  if (plan.nwm <= 1) {
     static const int kWarps1[9] = {4, 4, 2, 2, 2, 2, 1, 2, 1};
     plan.variant = (int)env_int("NVM_ATTN_DECODE_CFG", kDefaultDecodeVariant);
     if (plan.variant < 0 || plan.variant > 8 || plan.variant == 2 || plan.variant == 5) plan.variant = 3;
@@ -759,7 +951,7 @@ MmaPlan plan_paged_mma(const PagedArgs& a) {
     if (plan.variant < 0 || plan.variant > 3) plan.variant = 1;
     plan.nwk = kWarps3[plan.variant];
   }
-  plan.rows_per_block = 16 * plan.nwm;
+  plan.rows_per_block = plan.nwm == 0 ? 8 : 16 * plan.nwm;
   plan.n_row_blocks = (M + plan.rows_per_block - 1) / plan.rows_per_block;
   plan.rows_real = M < plan.rows_per_block ? M : plan.rows_per_block;
   plan.n_units = a.B * a.Hkv * plan.n_row_blocks;

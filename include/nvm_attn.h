@@ -26,6 +26,8 @@
  *   src/nano_vllm_metal/metal/src/flash_attention.cpp:17-61, 251-352
  *   src/nano_vllm_metal/cache/paged.py:152-195             (page write + int8 quantiser)
  *   src/nano_vllm_metal/cache/paged.py:60-70, 424-459      (page allocation on append)
+ *   src/nano_vllm_metal/cache/paged.py:197-210, 305-328, 530-559 (free, prefix attach,
+ *                                                            rewind, release)
  *   src/nano_vllm_metal/models/qwen3.py:100-116            (q/k norm, RoPE, cache update)
  *   src/nano_vllm_metal/layers/layernorm.py:4-14, layers/rotary_embedding.py:74-124
  */
@@ -253,6 +255,39 @@ int nvm_paged_append(int32_t* block_table, int32_t* context_lens, const int32_t*
                      int32_t* page_refcount, int64_t* slot_mapping, int64_t slot_capacity,
                      int32_t* status, int64_t B, int64_t max_pages, int64_t page_size,
                      int64_t capacity, void* stream);
+
+/*
+ * Batched rewind / release on the device.  Replaces, for b = 0..B-1 in order,
+ * TinyKvPagedCache.rewind(n) (src/nano_vllm_metal/cache/paged.py:530-550; n equal to
+ * the request's length is release(), paged.py:552-559) with TinyKvPagedPool.free_page
+ * (paged.py:197-210) -- e.g. dropping the rejected draft tokens of a batched
+ * speculative verify (engine/generate.py:55-169), or finishing requests.
+ *
+ * Request b drops rewind[b] tokens (0 <= rewind[b] <= context_lens[b]).  Pages past
+ * the new length lose one reference each (release walks the row forward, rewind pops
+ * it from the end); a page whose count reaches zero is pushed on the free stack at the
+ * position of the reference's sequential call that freed it.  Freed block-table
+ * entries become -1, context_lens[b] -= rewind[b].  last_call is [capacity] int32
+ * scratch holding -1 (and left so).  Invalid lengths or page ids set *status =
+ * NVM_ERR_INVALID_ARGUMENT before anything is written.  Single CTA; B <= 4096.
+ */
+int nvm_paged_rewind(int32_t* block_table, int32_t* context_lens, const int32_t* rewind,
+                     int32_t* free_stack, int32_t* free_top, int32_t* page_refcount,
+                     int32_t* last_call, int32_t* status, int64_t B, int64_t max_pages,
+                     int64_t page_size, int64_t capacity, void* stream);
+
+/*
+ * Prefix attach on the device: PrefixCache.attach (src/nano_vllm_metal/cache/paged.py:
+ * 305-328) for one layer's pool.  Fresh request b (no pages, length 0) with
+ * count[b] > 0 takes the shared full pages pages[b, 0:count[b]] (row width
+ * max_prefix): block_table[b, k] = pages[b, k], each page gains one reference,
+ * context_lens[b] = count[b] * page_size.  A non-fresh row or an invalid page sets
+ * *status = NVM_ERR_INVALID_ARGUMENT before anything is written.
+ */
+int nvm_paged_attach(int32_t* block_table, int32_t* context_lens, const int32_t* pages,
+                     const int32_t* count, int32_t* page_refcount, int32_t* status, int64_t B,
+                     int64_t max_pages, int64_t page_size, int64_t max_prefix, int64_t capacity,
+                     void* stream);
 
 #ifdef __cplusplus
 }

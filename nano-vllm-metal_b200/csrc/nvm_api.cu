@@ -298,4 +298,28 @@ int nvm_paged_append(int32_t* block_table, int32_t* context_lens, const int32_t*
                              static_cast<cudaStream_t>(stream));
 }
 
+int nvm_paged_rewind(int32_t* block_table, int32_t* context_lens, const int32_t* rewind, int32_t* free_stack,
+                     int32_t* free_top, int32_t* page_refcount, int32_t* last_call, int32_t* status, int64_t B,
+                     int64_t max_pages, int64_t page_size, int64_t capacity, void* stream) {
+  if (B < 0 || B > 4096 || max_pages < 0 || page_size <= 0 || capacity < 0)
+    return fail(NVM_ERR_INVALID_ARGUMENT, "rewind: invalid sizes (B must be in [0, 4096])");
+  if (B == 0) return NVM_OK;
+  if (!block_table || !context_lens || !rewind || !free_stack || !free_top || !page_refcount || !last_call || !status)
+    return fail(NVM_ERR_INVALID_ARGUMENT, "rewind: null tensor pointer");
+  return launch_paged_rewind(block_table, context_lens, rewind, free_stack, free_top, page_refcount, last_call, status,
+                             B, max_pages, page_size, capacity, static_cast<cudaStream_t>(stream));
+}
+
+int nvm_paged_attach(int32_t* block_table, int32_t* context_lens, const int32_t* pages, const int32_t* count,
+                     int32_t* page_refcount, int32_t* status, int64_t B, int64_t max_pages, int64_t page_size,
+                     int64_t max_prefix, int64_t capacity, void* stream) {
+  if (B < 0 || B > 4096 || max_pages < 0 || page_size <= 0 || max_prefix < 0 || capacity < 0)
+    return fail(NVM_ERR_INVALID_ARGUMENT, "attach: invalid sizes (B must be in [0, 4096])");
+  if (B == 0) return NVM_OK;
+  if (!block_table || !context_lens || !count || !page_refcount || !status || (max_prefix > 0 && !pages))
+    return fail(NVM_ERR_INVALID_ARGUMENT, "attach: null tensor pointer");
+  return launch_paged_attach(block_table, context_lens, pages, count, page_refcount, status, B, max_pages, page_size,
+                             max_prefix, capacity, static_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"

@@ -103,6 +103,12 @@ int launch_paged_append(int32_t* block_table, int32_t* context_lens, const int32
                         int32_t* free_stack, int32_t* free_top, int32_t* num_pages,
                         int32_t* page_refcount, int64_t* slot_mapping, int64_t slot_capacity, int32_t* status, int64_t B,
                         int64_t max_pages, int64_t page_size, int64_t capacity, cudaStream_t s);
+int launch_paged_rewind(int32_t* block_table, int32_t* context_lens, const int32_t* rewind, int32_t* free_stack,
+                        int32_t* free_top, int32_t* page_refcount, int32_t* last_call, int32_t* status, int64_t B,
+                        int64_t max_pages, int64_t page_size, int64_t capacity, cudaStream_t s);
+int launch_paged_attach(int32_t* block_table, int32_t* context_lens, const int32_t* pages, const int32_t* count,
+                        int32_t* page_refcount, int32_t* status, int64_t B, int64_t max_pages, int64_t page_size,
+                        int64_t max_prefix, int64_t capacity, cudaStream_t s);
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
 int encode_tmap(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* base,

@@ -485,6 +485,7 @@ class DevicePageTable:
         self.free_top = torch.zeros(1, **i32)
         self.num_pages = torch.zeros(1, **i32)
         self.refcount = torch.zeros(max(capacity, 1), **i32)
+        self.last_call = torch.full((max(capacity, 1),), -1, **i32)  # rewind scratch, kept at -1
         self.status = torch.zeros(1, **i32)
 
     def append(self, new_tokens: torch.Tensor, slot_mapping: torch.Tensor | None = None) -> torch.Tensor:
@@ -505,7 +506,47 @@ class DevicePageTable:
                 self.capacity, nv.stream_ptr(self.device)))
         return slot_mapping
 
+    def rewind(self, n_tokens: torch.Tensor) -> None:
+        """Drop ``n_tokens[b]`` tokens from the end of every request at once on the device:
+        the reference's ``TinyKvPagedCache.rewind`` for b = 0..B-1 in order
+        (``paged.py:530-550``; dropping a request's whole length is ``release``,
+        ``paged.py:552-559``).  Pages past the new lengths lose a reference and return to
+        the free stack, in the reference's order, when their count reaches zero."""
+        n = n_tokens.to(device=self.device, dtype=torch.int32).contiguous()
+        with torch.cuda.device(self.device):
+            nv.check(nv.lib().nvm_paged_rewind(
+                self.block_table.data_ptr(), self.context_lens.data_ptr(), n.data_ptr(), self.free_stack.data_ptr(),
+                self.free_top.data_ptr(), self.refcount.data_ptr(), self.last_call.data_ptr(),
+                self.status.data_ptr(), self.B, self.max_pages, self.page_size, self.capacity,
+                nv.stream_ptr(self.device)))
+
+    def release(self, mask: torch.Tensor | None = None) -> None:
+        """Release requests (all, or those where ``mask`` is true): rewind by their length."""
+        n = self.context_lens.clone()
+        if mask is not None:
+            n = torch.where(mask.to(device=self.device, dtype=torch.bool), n, torch.zeros_like(n))
+        self.rewind(n)
+
+    def attach(self, pages: torch.Tensor, count: torch.Tensor) -> None:
+        """``PrefixCache.attach`` on the device (``paged.py:305-328``): fresh request b
+        takes the shared full pages ``pages[b, :count[b]]`` (each gains a reference) and
+        starts at length ``count[b] * page_size``."""
+        pg = pages.to(device=self.device, dtype=torch.int32).contiguous()
+        ct = count.to(device=self.device, dtype=torch.int32).contiguous()
+        if pg.dim() != 2 or pg.shape[0] != self.B or ct.numel() != self.B:
+            raise ValueError("attach: pages must be [B, max_prefix] and count [B]")
+        with torch.cuda.device(self.device):
+            nv.check(nv.lib().nvm_paged_attach(
+                self.block_table.data_ptr(), self.context_lens.data_ptr(), pg.data_ptr(), ct.data_ptr(),
+                self.refcount.data_ptr(), self.status.data_ptr(), self.B, self.max_pages, self.page_size,
+                pg.shape[1], self.capacity, nv.stream_ptr(self.device)))
+
+    def free_list(self) -> list[int]:
+        """The free stack bottom to top (the next page taken is the last entry)."""
+        return self.free_stack[: int(self.free_top.item())].tolist()
+
     def check_status(self) -> None:
         st = int(self.status.item())
         if st != 0:
-            raise RuntimeError(f"allocate_page: device allocation failed ({st}: out of pages or block-table row full)")
+            raise RuntimeError(f"page table: device call failed (status {st}: out of pages, block-table row full, "
+                               "or an invalid rewind / attach)")

@@ -447,6 +447,16 @@ class PagedCacheRef:
         self.page_lens.clear()
         self.offset = 0
 
+    def attach(self, pages: list[int]) -> None:
+        """PrefixCache.attach for this layer (paged.py:305-328): a fresh cache takes shared
+        full pages, each gaining a reference."""
+        assert self.offset == 0 and self.num_pages == 0, "attach expects a fresh cache"
+        for pid in pages:
+            self.pool.incref(pid)
+            self.page_ids.append(pid)
+            self.page_lens.append(self.page_size)
+        self.offset = len(pages) * self.page_size
+
 
 class PagedStoreRef:
     """Numpy page storage with the reference's semantics (paged.py:96-195,461-475).

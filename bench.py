@@ -16,7 +16,8 @@ ranks / max-over-ranks time (strong scaling: the job is fixed as N grows).
 
 Secondary lines (N=1 only) time configs 1, 4, 5 (decode GB/s), 2a / 2b (prefill
 TFLOPS) and the fused q/k-norm + RoPE + K/V write at the 2a token count (GB/s) one
-launch at a time with an L2 flush between launches.
+launch at a time with an L2 flush between launches, and the per-decode-step batch
+metadata path (host wall time, device tables vs per-request host bookkeeping).
 """
 
 from __future__ import annotations
@@ -385,7 +386,69 @@ def secondary_results(peaks: dict, device) -> list[dict]:
                         roofline_frac=round(tf / peaks["bf16"], 4)))
         del w
     res.extend(qk_prep_results(peaks, device, flush))
+    res.append(metadata_results(device))
     return res
+
+
+def metadata_results(device, B: int = 256, ctx: int = 1024, steps: int = 20) -> dict:
+    """Secondary line: one decode step's batch metadata + K/V write for B requests of ctx
+    tokens (1 new token each, Qwen3-4B kv heads 8, d 128, bf16, page 16), host wall time
+    per step (synchronised).  Host path: the reference-shaped per-request bookkeeping
+    (BatchingKvCache.update_and_fetch_paged: Python loop over requests, block-table rows
+    rebuilt from lists and copied to the device).  Device path: DevicePageTable.append
+    (one kernel: new pages, slots, block tables, lengths) + the same scatter-write."""
+    from nano_vllm_b200 import BatchingKvCache, DevicePageTable, TinyKvPagedCache, TinyKvPagedPool, write_slots
+
+    Hkv, D, ps = 8, 128, 16
+    gen = torch.Generator(device=device)
+    gen.manual_seed(3)
+    k1 = torch.randn(B, Hkv, 1, D, generator=gen, device=device).bfloat16()
+    v1 = torch.randn(B, Hkv, 1, D, generator=gen, device=device).bfloat16()
+    # host path state
+    pool = TinyKvPagedPool(page_size=ps, device=device)
+    batch = BatchingKvCache(B, ctx + steps + 8)
+    for b in range(B):
+        c = TinyKvPagedCache(pool)
+        c.plan_append(ctx)
+        batch.add_request(c, b)
+    pool._ensure_page_storage(k1[:1])
+    torch.cuda.synchronize()
+
+    def host_step():
+        batch.update_and_fetch_paged(k1, v1)
+        torch.cuda.synchronize()
+
+    # device path state (same pool shape)
+    mp = (ctx + steps + 8 + ps - 1) // ps + 1
+    dt = DevicePageTable(B, mp, ps, B * mp + 16, device=device)
+    dt.append(torch.full((B,), ctx, dtype=torch.int32, device=device))
+    dt.check_status()
+    kp = torch.zeros(B * mp + 16, Hkv, ps, D, dtype=torch.bfloat16, device=device)
+    vp = torch.zeros_like(kp)
+    ones = torch.ones(B, dtype=torch.int32, device=device)
+    slots = torch.empty(B, dtype=torch.int64, device=device)
+    kt, vt = k1[:, :, 0], v1[:, :, 0]
+
+    def device_step():
+        dt.append(ones, slot_mapping=slots)
+        write_slots(kt, vt, slots, kp, vp)
+        torch.cuda.synchronize()
+
+    out = {}
+    for name, fn in (("host", host_step), ("device", device_step)):
+        for _ in range(3):
+            fn()
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            fn()
+        out[name] = (time.perf_counter() - t0) / steps * 1e6
+    dt.check_status()
+    del kp, vp, pool, batch
+    torch.cuda.empty_cache()
+    return dict(workload=f"decode-step batch metadata + K/V write, B={B}, ctx {ctx}, 1 new token, kv heads 8, d 128",
+                metric="host wall us per decode step", value=round(out["device"], 1), unit="us",
+                host_path_us=round(out["host"], 1), speedup=round(out["host"] / out["device"], 1),
+                higher_is_better=False)
 
 
 def qk_prep_bytes(T: int, Hq: int, Hkv: int, D: int, kv_bytes: int, scale_bytes: int) -> int:

@@ -3,7 +3,8 @@
  * nano-vllm-metal: paged-attention decode / multi-query, dense flash attention,
  * the paged KV scatter-write (with int8 quantise-on-write), device-side page
  * allocation for a batch of appends, and the fused per-layer q/k RMSNorm + RoPE +
- * K/V write that precedes every attention call.
+ * K/V write that precedes every attention call, and the 4-bit (W4A16) matmul of the
+ * projections around it.
  *
  * Conventions shared by every entry point
  *   - All tensor arguments are raw DEVICE pointers to row-major contiguous memory
@@ -30,6 +31,7 @@
  *                                                            rewind, release)
  *   src/nano_vllm_metal/models/qwen3.py:100-116            (q/k norm, RoPE, cache update)
  *   src/nano_vllm_metal/layers/layernorm.py:4-14, layers/rotary_embedding.py:74-124
+ *   src/nano_vllm_metal/metal/src/quantized_matmul.cpp:7-270  (W4A16 matmul)
  */
 #ifndef NVM_ATTN_H_
 #define NVM_ATTN_H_
@@ -288,6 +290,23 @@ int nvm_paged_attach(int32_t* block_table, int32_t* context_lens, const int32_t*
                      const int32_t* count, int32_t* page_refcount, int32_t* status, int64_t B,
                      int64_t max_pages, int64_t page_size, int64_t max_prefix, int64_t capacity,
                      void* stream);
+
+/* ------------------------------------------------------------------------- */
+/* W4A16 quantized matmul (4-bit weights, group 128)                          */
+/* ------------------------------------------------------------------------- */
+/*
+ * Replaces QuantizedMatmul (src/nano_vllm_metal/metal/src/quantized_matmul.cpp:7-270;
+ * Metal kernels quantized_matmul.metal:5-123; caller layers/linear.py:73-126):
+ *   out[m, k] = sum_n a[m, n] * (q[k, n] * scales[k, n / 128] + biases[k, n / 128])
+ * a [M, N] and out [M, K] in `dtype` (NVM_F16 / NVM_BF16, row-major), w [K, N / 8]
+ * uint32 with element n of a word in bits 4 (n % 8) .. 4 (n % 8) + 3, scales and
+ * biases [K, N / 128] in `dtype`; fp32 accumulation, the result rounded to `dtype`.
+ * group_size must be 128 and bits 4 (as the reference), N a multiple of 128, a and w
+ * 16-byte aligned.  Weights are read once per 16 rows of a.
+ */
+int nvm_w4a16_matmul(const void* a, int dtype, const uint32_t* w, const void* scales,
+                     const void* biases, void* out, int64_t M, int64_t N, int64_t K,
+                     int64_t group_size, int64_t bits, void* stream);
 
 #ifdef __cplusplus
 }

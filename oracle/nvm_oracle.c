@@ -530,3 +530,37 @@ int oracle_qk_norm_rope_write(const void* q, const void* k, const void* v, int d
   free(y);
   return err;
 }
+
+/*
+ * QuantizedMatmul::eval_cpu -- src/nano_vllm_metal/metal/src/quantized_matmul.cpp:80-148.
+ * a [M, N] and out [M, K] of dtype (F16 / BF16), b [K, N / 8] uint32 (element n of a
+ * word: bits 4 (n % 8) .. +3), scales / biases [K, N / 128] of dtype.  For every (i, k):
+ * sum over groups in order, inside a group over the words in order and the 8 nibbles of
+ * a word in order: w = nibble * scale + bias (fp32), sum += a * w (fp32); out rounded.
+ */
+void oracle_quantized_matmul(const void* a, int dtype, const uint32_t* b, const void* scales, const void* biases,
+                             void* out, int64_t M, int64_t N, int64_t K, int nthreads) {
+  const int64_t groups = N / 128;
+  set_threads(nthreads);
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < M; i++) {
+    for (int64_t k = 0; k < K; k++) {
+      float sum = 0.0f;
+      for (int64_t gi = 0; gi < groups; gi++) {
+        const float scale = load_elem(scales, k * groups + gi, dtype);
+        const float bias = load_elem(biases, k * groups + gi, dtype);
+        for (int64_t wd = 0; wd < 16; wd++) {
+          const uint32_t word = b[(k * N + gi * 128) / 8 + wd];
+          for (int j = 0; j < 8; j++) {
+            const float q = (float)((word >> (4 * j)) & 15u);
+            const float w = q * scale + bias;
+            const float av = load_elem(a, i * N + gi * 128 + wd * 8 + j, dtype);
+            sum = sum + av * w;
+          }
+        }
+      }
+      store_elem(out, i * K + k, dtype, sum);
+    }
+  }
+}
+

@@ -64,6 +64,7 @@ def lib():
         _lib.oracle_qk_norm_rope_write.argtypes = [P, P, P, I, P, P, F, P, P, I64, I, P, P, P, P, I, P, P, I, P,
                                                    I64, I64, I64, I64, I64, I64]
         _lib.oracle_qk_norm_rope_write.restype = ctypes.c_int
+        _lib.oracle_quantized_matmul.argtypes = [P, I, P, P, P, P, I64, I64, I64, I]
         _lib.oracle_max_threads.restype = ctypes.c_int
     return _lib
 
@@ -324,6 +325,40 @@ def qk_norm_rope_write_ref(q, k, v, dtype_code, wq, wk, eps, cos_t, sin_t, tradi
         None if k_scales is None else _ptr(k_scales), None if v_scales is None else _ptr(v_scales), scale_code,
         _ptr(sl), T, Hq, Hkv, D, P, ps)
     return q_out, int(err)
+
+
+# ---------------------------------------------------------------------------
+# W4A16 quantized matmul
+# ---------------------------------------------------------------------------
+
+def quantized_matmul_ref(a, dtype_code, b, scales, biases, nthreads=1):
+    """QuantizedMatmul::eval_cpu (quantized_matmul.cpp:80-148).  a [M, N] raw (uint16
+    bits for bf16), b [K, N / 8] uint32, scales / biases [K, N / 128] raw.  Returns the
+    raw [M, K] output."""
+    a = np.ascontiguousarray(a)
+    b = np.ascontiguousarray(b, dtype=np.uint32)
+    sc = np.ascontiguousarray(scales)
+    bi = np.ascontiguousarray(biases)
+    M, N = a.shape
+    K = b.shape[0]
+    out = np.empty((M, K), dtype=a.dtype)
+    lib().oracle_quantized_matmul(_ptr(a), dtype_code, _ptr(b), _ptr(sc), _ptr(bi), _ptr(out), M, N, K, nthreads)
+    return out
+
+
+def quantize_w4_ref(w: np.ndarray, group_size: int = 128):
+    """Affine 4-bit quantisation of float32 weights [K, N] per group: scale = (max - min) / 15,
+    bias = min, q = round((w - bias) / scale) clipped to [0, 15]; returns (packed uint32
+    [K, N / 8], scales, biases) as float32 (test-input generator, not the reference's)."""
+    K, N = w.shape
+    g = w.reshape(K, N // group_size, group_size)
+    lo, hi = g.min(-1), g.max(-1)
+    scale = np.where(hi > lo, (hi - lo) / 15.0, 1.0).astype(np.float32)
+    q = np.clip(np.rint((g - lo[..., None]) / scale[..., None]), 0, 15).astype(np.uint32).reshape(K, N)
+    packed = np.zeros((K, N // 8), dtype=np.uint32)
+    for j in range(8):
+        packed |= q[:, j::8] << np.uint32(4 * j)
+    return packed, scale, lo.astype(np.float32)
 
 
 # ---------------------------------------------------------------------------

@@ -16,8 +16,9 @@ ranks / max-over-ranks time (strong scaling: the job is fixed as N grows).
 
 Secondary lines (N=1 only) time configs 1, 4, 5 (decode GB/s), 2a / 2b (prefill
 TFLOPS) and the fused q/k-norm + RoPE + K/V write at the 2a token count (GB/s) one
-launch at a time with an L2 flush between launches, and the per-decode-step batch
-metadata path (host wall time, device tables vs per-request host bookkeeping).
+launch at a time with an L2 flush between launches, the per-decode-step batch metadata
+path (host wall time, device tables vs per-request host bookkeeping) and the W4A16
+matmul at Qwen3-4B's MLP shapes (GB/s).
 """
 
 from __future__ import annotations
@@ -387,6 +388,33 @@ def secondary_results(peaks: dict, device) -> list[dict]:
         del w
     res.extend(qk_prep_results(peaks, device, flush))
     res.append(metadata_results(device))
+    res.extend(w4a16_results(peaks, device, flush))
+    return res
+
+
+def w4a16_results(peaks: dict, device, flush) -> list[dict]:
+    """Secondary lines: W4A16 (4-bit, group 128) matmul at Qwen3-4B's decode shapes
+    (gate+up projection K = 2 x 9728, N = 2560; down projection K = 2560, N = 9728),
+    M = 1 and 8 activation rows, bf16; GB/s of weights + scales + biases + activations."""
+    from nano_vllm_b200.layers.linear import quantized_matmul
+
+    res = []
+    gen = torch.Generator(device=device)
+    gen.manual_seed(11)
+    for name, K, N in [("gate_up", 2 * 9728, 2560), ("down", 2560, 9728)]:
+        w = torch.randint(-2 ** 31, 2 ** 31 - 1, (K, N // 8), generator=gen, dtype=torch.int64,
+                          device=device).to(torch.int32)
+        s = (torch.rand(K, N // 128, generator=gen, device=device) * 0.02).bfloat16()
+        b = (torch.rand(K, N // 128, generator=gen, device=device) * -0.1).bfloat16()
+        for M in (1, 8):
+            a = torch.randn(M, N, generator=gen, device=device).bfloat16()
+            nbytes = K * N // 2 + 2 * K * (N // 128) * 2 + M * N * 2 + M * K * 2
+            ms = statistics.median(time_launches(lambda: quantized_matmul(s, b, 128, 4, a, w, True), 20, 3, flush))
+            gbs = nbytes / (ms * 1e-3) / 1e9
+            res.append(dict(workload=f"W4A16 matmul {name} Qwen3-4B (K={K}, N={N}), M={M}, bf16",
+                            metric="w4a16 GB/s", value=round(gbs, 1), unit="GB/s", ms=round(ms, 4), bytes=nbytes,
+                            roofline_frac=round(gbs / peaks["hbm"], 4), l2="flushed"))
+        del w, s, b
     return res
 
 

@@ -14,8 +14,8 @@
 // applied once per group in fp32.  A warp streams a 16-row x 128-element tile (1 KB of
 // packed weights, two full 32-byte sectors per row) per group, the nibbles turned into
 // bf16 / fp16 pairs with one LOP3 + one subtract per pair (magic-exponent trick), the
-// next group's weights loaded before the current one is multiplied.  A CTA's 8 warps
-// split the groups of its 16 rows and reduce in shared memory.  Weights are read once for
+// weights of four groups loaded before the first is multiplied.  A CTA's 16 warps split
+// the groups of its 16 rows and reduce in shared memory.  Weights are read once for
 // up to 16 activation rows; the kernel is bound by HBM bytes (0.53 B per weight).
 #include <cstdint>
 
@@ -25,7 +25,8 @@
 namespace nvm {
 namespace {
 
-constexpr int kWarps = 8;
+constexpr int kWarps = 16;
+constexpr int kPF = 4;      // groups whose weights a warp loads before using any
 constexpr int kRows = 16;   // output rows (weight rows) per CTA
 constexpr int kGroup = 128;
 
@@ -106,66 +107,72 @@ __global__ void __launch_bounds__(kWarps * 32) w4a16_kernel(const W4Params p) {
 #pragma unroll
   for (int n = 0; n < NT; ++n) tot[n][0] = tot[n][1] = tot[n][2] = tot[n][3] = 0.f;
 
-  auto load_w = [&](int64_t grp, uint4& a4, uint4& b4) {
-    a4 = okA ? __ldg(wA + grp * 4) : make_uint4(0, 0, 0, 0);
-    b4 = okB ? __ldg(wB + grp * 4) : make_uint4(0, 0, 0, 0);
-  };
-  uint4 nwA, nwB;
-  int64_t grp = warp;
-  if (grp < G) load_w(grp, nwA, nwB);
-  for (; grp < G; grp += kWarps) {
-    const uint4 cwA = nwA, cwB = nwB;
-    if (grp + kWarps < G) load_w(grp + kWarps, nwA, nwB);
-    // activations of this group: row mb + 8n + g, elements [32 t, 32 t + 32)
-    uint4 av[NT][4];
-    float asum_own[NT];
+  // kPF groups per warp in flight: their weight loads are issued before any of them is used
+  for (int64_t base = warp; base < G; base += (int64_t)kWarps * kPF) {
+    uint4 cwA[kPF], cwB[kPF];
 #pragma unroll
-    for (int n = 0; n < NT; ++n) {
-      const int64_t m = mb + 8 * n + g;
-      const uint4* ap = reinterpret_cast<const uint4*>(act + (m < p.M ? m : 0) * p.N + grp * kGroup + 32 * t);
-      float s = 0.f;
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        av[n][q] = m < p.M ? __ldg(ap + q) : make_uint4(0, 0, 0, 0);
-        const T* e = reinterpret_cast<const T*>(&av[n][q]);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) s += to_f32(e[i]);
-      }
-      asum_own[n] = s;
+    for (int i = 0; i < kPF; ++i) {
+      const int64_t grp = base + (int64_t)i * kWarps;
+      const bool ok = grp < G;
+      cwA[i] = ok && okA ? __ldg(wA + grp * 4) : make_uint4(0, 0, 0, 0);
+      cwB[i] = ok && okB ? __ldg(wB + grp * 4) : make_uint4(0, 0, 0, 0);
     }
-    // the group's products: two accumulator chains per n-tile
-    float acc[NT][2][4];
 #pragma unroll
-    for (int n = 0; n < NT; ++n)
+    for (int i = 0; i < kPF; ++i) {
+      const int64_t grp = base + (int64_t)i * kWarps;
+      if (grp >= G) break;  // warp-uniform
+      // activations of this group: row mb + 8n + g, elements [32 t, 32 t + 32)
+      uint4 av[NT][4];
+      float asum_own[NT];
 #pragma unroll
-      for (int c = 0; c < 2; ++c) acc[n][c][0] = acc[n][c][1] = acc[n][c][2] = acc[n][c][3] = 0.f;
-    const uint32_t xa[4] = {cwA.x, cwA.y, cwA.z, cwA.w}, xb[4] = {cwB.x, cwB.y, cwB.z, cwB.w};
+      for (int n = 0; n < NT; ++n) {
+        const int64_t m = mb + 8 * n + g;
+        const uint4* ap = reinterpret_cast<const uint4*>(act + (m < p.M ? m : 0) * p.N + grp * kGroup + 32 * t);
+        float sm = 0.f;
 #pragma unroll
-    for (int w = 0; w < 4; ++w) {
+        for (int q = 0; q < 4; ++q) {
+          av[n][q] = m < p.M ? __ldg(ap + q) : make_uint4(0, 0, 0, 0);
+          const T* e = reinterpret_cast<const T*>(&av[n][q]);
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int jl = 2 * h, jh = 2 * h + 1;  // low / high pair of k-step 2w + h
-        const uint32_t afr[4] = {nib_pair<T>(xa[w], jl), nib_pair<T>(xb[w], jl), nib_pair<T>(xa[w], jh),
-                                 nib_pair<T>(xb[w], jh)};
-#pragma unroll
-        for (int n = 0; n < NT; ++n) Tr::mma(acc[n][h], afr, act_pair(av[n][w], jl), act_pair(av[n][w], jh));
+          for (int j = 0; j < 8; ++j) sm += to_f32(e[j]);
+        }
+        asum_own[n] = sm;
       }
-    }
-    // per-group scale and bias: rows g / g + 8, activation rows 2t / 2t + 1
-    const float sA = okA ? to_f32(sc[rA * G + grp]) : 0.f, bA = okA ? to_f32(bi[rA * G + grp]) : 0.f;
-    const float sB = okB ? to_f32(sc[rB * G + grp]) : 0.f, bB = okB ? to_f32(bi[rB * G + grp]) : 0.f;
+      // the group's products: two accumulator chains per n-tile
+      float acc[NT][2][4];
 #pragma unroll
-    for (int n = 0; n < NT; ++n) {
-      float as = asum_own[n];
-      as += __shfl_xor_sync(0xffffffffu, as, 1);
-      as += __shfl_xor_sync(0xffffffffu, as, 2);  // every lane of quad g: sum for row 8n + g
-      const float s0 = __shfl_sync(0xffffffffu, as, 8 * t), s1 = __shfl_sync(0xffffffffu, as, 8 * t + 4);
-      const float d0 = acc[n][0][0] + acc[n][1][0], d1 = acc[n][0][1] + acc[n][1][1];
-      const float d2 = acc[n][0][2] + acc[n][1][2], d3 = acc[n][0][3] + acc[n][1][3];
-      tot[n][0] += sA * d0 + bA * s0;
-      tot[n][1] += sA * d1 + bA * s1;
-      tot[n][2] += sB * d2 + bB * s0;
-      tot[n][3] += sB * d3 + bB * s1;
+      for (int n = 0; n < NT; ++n)
+#pragma unroll
+        for (int c = 0; c < 2; ++c) acc[n][c][0] = acc[n][c][1] = acc[n][c][2] = acc[n][c][3] = 0.f;
+      const uint32_t xa[4] = {cwA[i].x, cwA[i].y, cwA[i].z, cwA[i].w};
+      const uint32_t xb[4] = {cwB[i].x, cwB[i].y, cwB[i].z, cwB[i].w};
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int jl = 2 * h, jh = 2 * h + 1;  // low / high pair of k-step 2w + h
+          const uint32_t afr[4] = {nib_pair<T>(xa[w], jl), nib_pair<T>(xb[w], jl), nib_pair<T>(xa[w], jh),
+                                   nib_pair<T>(xb[w], jh)};
+#pragma unroll
+          for (int n = 0; n < NT; ++n) Tr::mma(acc[n][h], afr, act_pair(av[n][w], jl), act_pair(av[n][w], jh));
+        }
+      }
+      // per-group scale and bias: rows g / g + 8, activation rows 2t / 2t + 1
+      const float sA = okA ? to_f32(sc[rA * G + grp]) : 0.f, bA = okA ? to_f32(bi[rA * G + grp]) : 0.f;
+      const float sB = okB ? to_f32(sc[rB * G + grp]) : 0.f, bB = okB ? to_f32(bi[rB * G + grp]) : 0.f;
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+        float as = asum_own[n];
+        as += __shfl_xor_sync(0xffffffffu, as, 1);
+        as += __shfl_xor_sync(0xffffffffu, as, 2);  // every lane of quad g: sum for row 8n + g
+        const float s0 = __shfl_sync(0xffffffffu, as, 8 * t), s1 = __shfl_sync(0xffffffffu, as, 8 * t + 4);
+        const float d0 = acc[n][0][0] + acc[n][1][0], d1 = acc[n][0][1] + acc[n][1][1];
+        const float d2 = acc[n][0][2] + acc[n][1][2], d3 = acc[n][0][3] + acc[n][1][3];
+        tot[n][0] += sA * d0 + bA * s0;
+        tot[n][1] += sA * d1 + bA * s1;
+        tot[n][2] += sB * d2 + bB * s0;
+        tot[n][3] += sB * d3 + bB * s1;
+      }
     }
   }
   // reduce the warps' partial sums; fragment c0: (row g, act 2t), c1: (g, 2t+1),

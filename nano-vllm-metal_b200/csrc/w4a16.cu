@@ -14,7 +14,7 @@
 // applied once per group in fp32.  A warp streams a 16-row x 128-element tile (1 KB of
 // packed weights, two full 32-byte sectors per row) per group, the nibbles turned into
 // bf16 / fp16 pairs with one LOP3 + one subtract per pair (magic-exponent trick), the
-// weights of four groups loaded before the first is multiplied.  A CTA's 16 warps split
+// weights of two groups loaded before the first is multiplied.  A CTA's 8 warps split
 // the groups of its 16 rows and reduce in shared memory.  Weights are read once for
 // up to 16 activation rows; the kernel is bound by HBM bytes (0.53 B per weight).
 #include <cstdint>
@@ -25,8 +25,8 @@
 namespace nvm {
 namespace {
 
-constexpr int kWarps = 16;
-constexpr int kPF = 4;      // groups whose weights a warp loads before using any
+constexpr int kWarps = 8;
+constexpr int kPF = 2;      // groups whose weights a warp loads before using any
 constexpr int kRows = 16;   // output rows (weight rows) per CTA
 constexpr int kGroup = 128;
 

@@ -246,6 +246,9 @@ def time_launches(fn, iters: int, warmup: int, flush_buf=None) -> list[float]:
     for _ in range(iters):
         if flush_buf is not None:
             flush_l2(flush_buf)
+        # keep the GPU busy (~50 us) while the host queues the start event and the
+        # launch, so host-side delays never show up as idle time inside the events
+        torch.cuda._sleep(100_000)
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record(stream)
         fn()
@@ -305,6 +308,9 @@ def cpu_baseline_decode(cfg: dict, w: dict | None, target_s: float = 10.0):
     host for the longest sampled context and reused, so generation stays outside the
     timed calls.
     """
+    # OpenMP worker threads must sleep, not spin, once the sample is done: spinning
+    # threads on every core delay the host's kernel launches in the GPU timings after it
+    os.environ.setdefault("OMP_WAIT_POLICY", "PASSIVE")
     from oracle import oracle as o
 
     nthreads = o.max_threads()

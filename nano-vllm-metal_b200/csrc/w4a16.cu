@@ -15,9 +15,14 @@
 // packed weights, two full 32-byte sectors per row) per group, the nibbles turned into
 // bf16 / fp16 pairs with one LOP3 + one subtract per pair (magic-exponent trick), the
 // weights of two groups loaded before the first is multiplied.  A CTA's 8 warps split
-// the groups of its 16 rows and reduce in shared memory.  Weights are read once for
+// the groups of its 16 rows and reduce in shared memory; when a projection has fewer
+// 16-row tiles than two per SM, the groups of a tile are further split over a cluster of
+// up to 8 CTAs whose partial sums are added in rank 0's shared memory (read over DSMEM).  Weights are read once for
 // up to 16 activation rows; the kernel is bound by HBM bytes (0.53 B per weight).
+#include <cooperative_groups.h>
+#include <algorithm>
 #include <cstdint>
+#include <cstdlib>
 
 #include "nvm_common.cuh"
 #include "nvm_internal.h"
@@ -26,6 +31,12 @@ namespace nvm {
 namespace {
 
 constexpr int kWarps = 8;
+
+int64_t env_int(const char* name, int64_t dflt) {
+  const char* v = std::getenv(name);
+  if (v == nullptr || v[0] == '\0') return dflt;
+  return std::atoll(v);
+}
 constexpr int kPF = 2;      // groups whose weights a warp loads before using any
 constexpr int kRows = 16;   // output rows (weight rows) per CTA
 constexpr int kGroup = 128;
@@ -86,10 +97,13 @@ __device__ __forceinline__ uint32_t act_pair(const uint4& v, int j) {
 // rows g and g + 8 of the CTA's tile and, in every group, elements [32 t, 32 t + 32)
 // as four words of eight nibbles; the mma's k index is permuted consistently in the
 // weights and the activations (pair (j, j + 4) of word w feeds k-step 2w + j / 2).
-template <typename T, int NT>
+// kCluster: the groups are split over the gridDim.z CTAs of a thread-block cluster (for
+// projections with few 16-row tiles); their partial sums meet in rank 0's shared memory.
+template <typename T, int NT, bool kCluster>
 __global__ void __launch_bounds__(kWarps * 32) w4a16_kernel(const W4Params p) {
   using Tr = W4Traits<T>;
   __shared__ float red[kWarps][32][4 * NT];
+  __shared__ float part[32][4 * NT];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const int64_t k0 = (int64_t)blockIdx.x * kRows;
@@ -107,19 +121,23 @@ __global__ void __launch_bounds__(kWarps * 32) w4a16_kernel(const W4Params p) {
 #pragma unroll
   for (int n = 0; n < NT; ++n) tot[n][0] = tot[n][1] = tot[n][2] = tot[n][3] = 0.f;
 
+  // warps of all CTAs of the split share the groups round-robin
+  const int64_t nsplit = kCluster ? gridDim.z : 1;
+  const int64_t wstride = (int64_t)kWarps * nsplit;
+  const int64_t wid = (kCluster ? (int64_t)blockIdx.z * kWarps : 0) + warp;
   // kPF groups per warp in flight: their weight loads are issued before any of them is used
-  for (int64_t base = warp; base < G; base += (int64_t)kWarps * kPF) {
+  for (int64_t base = wid; base < G; base += wstride * kPF) {
     uint4 cwA[kPF], cwB[kPF];
 #pragma unroll
     for (int i = 0; i < kPF; ++i) {
-      const int64_t grp = base + (int64_t)i * kWarps;
+      const int64_t grp = base + (int64_t)i * wstride;
       const bool ok = grp < G;
       cwA[i] = ok && okA ? __ldg(wA + grp * 4) : make_uint4(0, 0, 0, 0);
       cwB[i] = ok && okB ? __ldg(wB + grp * 4) : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
     for (int i = 0; i < kPF; ++i) {
-      const int64_t grp = base + (int64_t)i * kWarps;
+      const int64_t grp = base + (int64_t)i * wstride;
       if (grp >= G) break;  // warp-uniform
       // activations of this group: row mb + 8n + g, elements [32 t, 32 t + 32)
       uint4 av[NT][4];
@@ -182,32 +200,82 @@ __global__ void __launch_bounds__(kWarps * 32) w4a16_kernel(const W4Params p) {
 #pragma unroll
     for (int e = 0; e < 4; ++e) red[warp][lane][4 * n + e] = tot[n][e];
   __syncthreads();
-  T* out = static_cast<T*>(p.out);
   for (int idx = threadIdx.x; idx < 32 * 4 * NT; idx += kWarps * 32) {
     const int ln = idx / (4 * NT), ee = idx % (4 * NT);
     float s = 0.f;
 #pragma unroll
     for (int w = 0; w < kWarps; ++w) s += red[w][ln][ee];
+    part[ln][ee] = s;
+  }
+  // every CTA of a cluster reaches both cluster barriers (no early exit above)
+  namespace cg = cooperative_groups;
+  if constexpr (kCluster) cg::this_cluster().sync();
+  else __syncthreads();
+  const bool writer = kCluster ? cg::this_cluster().block_rank() == 0 : true;
+  T* out = static_cast<T*>(p.out);
+  for (int idx = threadIdx.x; writer && idx < 32 * 4 * NT; idx += kWarps * 32) {
+    const int ln = idx / (4 * NT), ee = idx % (4 * NT);
+    float s = part[ln][ee];
+    if constexpr (kCluster) {
+      for (unsigned r = 1; r < cg::this_cluster().num_blocks(); ++r)
+        s += cg::this_cluster().map_shared_rank(&part[0][0], r)[idx];
+    }
     const int n = ee / 4, e = ee % 4;
     const int gg = ln >> 2, tt = ln & 3;
     const int64_t row = k0 + gg + ((e & 2) ? 8 : 0);
     const int64_t m = mb + 8 * n + 2 * tt + (e & 1);
     if (row < p.K && m < p.M) out[m * p.K + row] = from_f32<T>(s);
   }
+  if constexpr (kCluster) cg::this_cluster().sync();  // peers keep their shared memory until read
+}
+
+int sm_count() {
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess && cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess)
+      sms = n;
+    if (sms <= 0) sms = 148;
+  }
+  return sms;
+}
+
+template <typename T, int NT>
+int launch_nt(const W4Params& base, unsigned gx, unsigned gy, cudaStream_t s) {
+  // Fewer 16-row tiles than two per SM: split every tile's groups over a cluster of up to
+  // 8 CTAs (each still with at least two groups per warp).
+  const int64_t G = base.N / kGroup;
+  int64_t split = (2LL * sm_count() + (int64_t)gx * gy - 1) / ((int64_t)gx * gy);
+  split = std::min<int64_t>(split, 8);
+  split = std::min<int64_t>(split, G / (2 * kWarps));
+  if (env_int("NVM_W4_SPLIT", 0) > 0) split = std::min<int64_t>(env_int("NVM_W4_SPLIT", 0), 8);
+  if (split <= 1) {
+    w4a16_kernel<T, NT, false><<<dim3(gx, gy), kWarps * 32, 0, s>>>(base);
+    return check_cuda(cudaGetLastError(), "quantized_matmul: kernel launch");
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(gx, gy, (unsigned)split);
+  cfg.blockDim = dim3(kWarps * 32, 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = (unsigned)split;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return check_cuda(cudaLaunchKernelEx(&cfg, w4a16_kernel<T, NT, true>, base), "quantized_matmul: kernel launch");
 }
 
 template <typename T>
 int launch_t(const W4Params& base, cudaStream_t s) {
   const unsigned gx = (unsigned)((base.K + kRows - 1) / kRows);
-  if (base.M <= 8) {
-    w4a16_kernel<T, 1><<<dim3(gx, 1), kWarps * 32, 0, s>>>(base);
-  } else {
-    // 16 activation rows per CTA; the weight tile is re-read (from L2) per 16 rows
-    const int64_t chunks = (base.M + 15) / 16;
-    if (chunks > 65535) return fail(NVM_ERR_INVALID_ARGUMENT, "quantized_matmul: too many rows");
-    w4a16_kernel<T, 2><<<dim3(gx, (unsigned)chunks), kWarps * 32, 0, s>>>(base);
-  }
-  return check_cuda(cudaGetLastError(), "quantized_matmul: kernel launch");
+  if (base.M <= 8) return launch_nt<T, 1>(base, gx, 1, s);
+  // 16 activation rows per CTA; the weight tile is re-read (from L2) per 16 rows
+  const int64_t chunks = (base.M + 15) / 16;
+  if (chunks > 65535) return fail(NVM_ERR_INVALID_ARGUMENT, "quantized_matmul: too many rows");
+  return launch_nt<T, 2>(base, gx, (unsigned)chunks, s);
 }
 
 }  // namespace

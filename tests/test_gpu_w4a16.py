@@ -85,3 +85,19 @@ def test_argument_errors(cuda):
         quantized_matmul(s, s, 128, 4, a, b, False)
     with pytest.raises(RuntimeError, match="same dtype as scales"):
         quantized_matmul(s, s, 128, 4, a.half(), b, True)
+
+
+@pytest.mark.parametrize("split", [1, 2, 3, 8])
+def test_cluster_split_matches_oracle(cuda, oracle, monkeypatch, split):
+    """The groups of each 16-row tile split over a thread-block cluster of `split` CTAs
+    (forced here; by default only projections with few tiles split) give the oracle's
+    result to the same tolerance, including ragged rows and a group count that does not
+    divide evenly."""
+    monkeypatch.setenv("NVM_W4_SPLIT", str(split))
+    rng = np.random.default_rng(split)
+    for M, N, K in [(3, 4096, 40), (12, 2560, 17)]:
+        t, ref = _problem(oracle, rng, M, N, K, torch.bfloat16, cuda)
+        out = quantized_matmul(t["s"], t["bi"], 128, 4, t["a"], t["b"], transpose_b=True)
+        got = oracle.to_f32(to_np(out), 2).astype(np.float64)
+        r = oracle.to_f32(ref, 2).astype(np.float64)
+        np.testing.assert_allclose(got, r, rtol=2.0 ** -7, atol=1e-4 * np.abs(r).max() + 1e-6)

@@ -125,6 +125,13 @@ SWEEP = [
     (torch.int8, 128, 16, 16, 4, 5, True),
     (torch.int8, 128, 32, 8, 8, 1, True),
     (torch.int8, 32, 4, 4, 2, 2, True),      # generic int8 path
+    # multi-token rows on the n8 tile (at most eight query rows per kv head, causal
+    # limits differing per row)
+    (torch.bfloat16, 128, 16, 8, 4, 3, True),
+    (torch.float16, 128, 16, 8, 2, 2, True),
+    (torch.int8, 128, 16, 8, 4, 3, True),
+    (torch.bfloat16, 64, 16, 4, 4, 5, True),
+    (torch.float16, 128, 32, 6, 2, 2, False),
 ]
 
 

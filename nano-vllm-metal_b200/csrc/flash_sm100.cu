@@ -191,7 +191,10 @@ __device__ __forceinline__ float ex2_ftz(float x) {
 }
 
 // Pairs q (keys 2q, 2q+1 of a 64-key tile) whose exponentials run on the FMA pipe.
-constexpr uint32_t kEmuPairs = 0x88888888u;  // every fourth pair: 25%
+// None by default: with two CTAs per SM the softmax warps are bound by instruction
+// issue, not by the MUFU unit, and the polynomial costs more issue slots than ex2
+// (measured: 25 % on the FMA pipe 730 TFLOP/s on config 2a, none 745, half 714).
+constexpr uint32_t kEmuPairs = 0x0u;
 
 // 2^x for two floats on the FMA pipe: n = round(x) through the 1.5 * 2^23 rounding
 // constant, f = x - n in [-0.5, 0.5] (exact), 2^f from a polynomial, then n is added to
@@ -854,9 +857,8 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         const float mu = m_ref == -INFINITY ? 0.f : m_ref;
         const float alpha = ex2_ftz(m - mu);  // 0 when m == -inf
-        // p = 2^(s * sl2 - mu) on packed pairs.  Most exponentials run on the MUFU unit;
-        // outside split tiles the pairs selected by kEmuPairs run on the FMA pipe instead
-        // (exp2_fma2), which keeps MUFU from setting the tile rate.
+        // p = 2^(s * sl2 - mu) on packed pairs, on the MUFU unit; outside split tiles the
+        // pairs selected by kEmuPairs (none by default) run on the FMA pipe (exp2_fma2).
         const float2 sl2v = make_float2(sl2, sl2), nmu = make_float2(-mu, -mu);
         float2 acc[4];
 #pragma unroll

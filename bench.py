@@ -394,6 +394,7 @@ def secondary_results(peaks: dict, device) -> list[dict]:
         del w
     res.extend(qk_prep_results(peaks, device, flush))
     res.append(metadata_results(device))
+    res.append(decode_step_results(device))
     res.extend(w4a16_results(peaks, device, flush))
     return res
 
@@ -422,6 +423,75 @@ def w4a16_results(peaks: dict, device, flush) -> list[dict]:
                             roofline_frac=round(gbs / peaks["hbm"], 4), l2="flushed"))
         del w, s, b
     return res
+
+
+def decode_step_results(device, layers: int = 36, B: int = 64, ctx: int = 1024, steps: int = 20) -> dict:
+    """Secondary line: the attention path of one decode step of a Qwen3-4B-shaped model
+    (36 layers, 32 q / 8 kv heads, d 128, bf16, page 16), B requests of ctx tokens, host
+    wall time per step: DevicePageTable.append once, then per layer the fused q/k norm +
+    RoPE + K/V write and paged attention, with the metadata on the device throughout --
+    launched eagerly, and as one CUDA graph replayed per step."""
+    from nano_vllm_b200 import DevicePageTable, paged_attention
+    from nano_vllm_b200.layers.qk_prep import qk_norm_rope_write
+    from nano_vllm_b200.layers.rotary_embedding import RoPE
+
+    Hq, Hkv, D, ps = 32, 8, 128, 16
+    gen = torch.Generator(device=device)
+    gen.manual_seed(17)
+    mp = (ctx + 3 * (steps + 4) + ps - 1) // ps + 1
+    cap = B * mp + 16
+    table = DevicePageTable(B, mp, ps, cap, device=device)
+    table.append(torch.full((B,), ctx, dtype=torch.int32, device=device))
+    table.check_status()
+    pools = [(torch.randn(cap, Hkv, ps, D, generator=gen, device=device).bfloat16(),
+              torch.randn(cap, Hkv, ps, D, generator=gen, device=device).bfloat16()) for _ in range(layers)]
+    qkv = torch.randn(layers, B, 1, (Hq + 2 * Hkv) * D, generator=gen, device=device).bfloat16()
+    wq = (torch.rand(D, generator=gen, device=device) + 0.5).bfloat16()
+    wk = (torch.rand(D, generator=gen, device=device) + 0.5).bfloat16()
+    rope = RoPE(D, 40960, 1000000, device=device)
+    ones = torch.ones(B, dtype=torch.int32, device=device)
+    slots = torch.empty(B, dtype=torch.int64, device=device)
+
+    def step():
+        table.append(ones, slot_mapping=slots)
+        pos = (table.context_lens - 1).view(B, 1)
+        for li in range(layers):
+            x = qkv[li]
+            q = x[..., :Hq * D].view(B, 1, Hq, D)
+            k = x[..., Hq * D:(Hq + Hkv) * D].view(B, 1, Hkv, D)
+            v = x[..., (Hq + Hkv) * D:].view(B, 1, Hkv, D)
+            kp, vp = pools[li]
+            qr = qk_norm_rope_write(q, k, v, wq, wk, rope, pos, kp, vp, slots, eps=1e-6)
+            paged_attention(qr, kp, vp, table.block_table, table.context_lens, ps, out_dtype=torch.bfloat16)
+
+    def eager():
+        step()
+        torch.cuda.synchronize()
+
+    for _ in range(3):
+        eager()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+
+    def replay():
+        graph.replay()
+        torch.cuda.synchronize()
+
+    out = {}
+    for name, fn in (("eager", eager), ("graph", replay)):
+        fn()
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            fn()
+        out[name] = (time.perf_counter() - t0) / steps * 1e6
+    table.check_status()
+    del graph, pools, qkv
+    torch.cuda.empty_cache()
+    return dict(workload=f"decode-step attention path, {layers} layers, B={B}, ctx {ctx}, Qwen3-4B heads, bf16: "
+                         f"device append + per layer fused prep + paged attention",
+                metric="host wall us per decode step", value=round(out["graph"], 1), unit="us",
+                eager_us=round(out["eager"], 1), higher_is_better=False)
 
 
 def metadata_results(device, B: int = 256, ctx: int = 1024, steps: int = 20) -> dict:

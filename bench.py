@@ -246,9 +246,9 @@ def time_launches(fn, iters: int, warmup: int, flush_buf=None) -> list[float]:
     for _ in range(iters):
         if flush_buf is not None:
             flush_l2(flush_buf)
-        # keep the GPU busy (~50 us) while the host queues the start event and the
+        # keep the GPU busy (~200 us) while the host queues the start event and the
         # launch, so host-side delays never show up as idle time inside the events
-        torch.cuda._sleep(100_000)
+        torch.cuda._sleep(400_000)
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record(stream)
         fn()
@@ -399,7 +399,8 @@ def secondary_results(peaks: dict, device) -> list[dict]:
     return res
 
 
-def w4a16_results(peaks: dict, device, flush) -> list[dict]:
+def w4a16_results(peaks: dict, device, flush, shapes=(("gate_up", 2 * 9728, 2560), ("down", 2560, 9728)),
+                  ms_rows=(1, 8), iters: int = 20, warmup: int = 3) -> list[dict]:
     """Secondary lines: W4A16 (4-bit, group 128) matmul at Qwen3-4B's decode shapes
     (gate+up projection K = 2 x 9728, N = 2560; down projection K = 2560, N = 9728),
     M = 1 and 8 activation rows, bf16; GB/s of weights + scales + biases + activations."""
@@ -408,15 +409,16 @@ def w4a16_results(peaks: dict, device, flush) -> list[dict]:
     res = []
     gen = torch.Generator(device=device)
     gen.manual_seed(11)
-    for name, K, N in [("gate_up", 2 * 9728, 2560), ("down", 2560, 9728)]:
+    for name, K, N in shapes:
         w = torch.randint(-2 ** 31, 2 ** 31 - 1, (K, N // 8), generator=gen, dtype=torch.int64,
                           device=device).to(torch.int32)
         s = (torch.rand(K, N // 128, generator=gen, device=device) * 0.02).bfloat16()
         b = (torch.rand(K, N // 128, generator=gen, device=device) * -0.1).bfloat16()
-        for M in (1, 8):
+        for M in ms_rows:
             a = torch.randn(M, N, generator=gen, device=device).bfloat16()
             nbytes = K * N // 2 + 2 * K * (N // 128) * 2 + M * N * 2 + M * K * 2
-            ms = statistics.median(time_launches(lambda: quantized_matmul(s, b, 128, 4, a, w, True), 20, 3, flush))
+            ms = statistics.median(time_launches(lambda: quantized_matmul(s, b, 128, 4, a, w, True), iters, warmup,
+                                                 flush))
             gbs = nbytes / (ms * 1e-3) / 1e9
             res.append(dict(workload=f"W4A16 matmul {name} Qwen3-4B (K={K}, N={N}), M={M}, bf16",
                             metric="w4a16 GB/s", value=round(gbs, 1), unit="GB/s", ms=round(ms, 4), bytes=nbytes,
@@ -636,6 +638,23 @@ def run_qkprep(args):
     print(json.dumps(line), flush=True)
 
 
+def run_w4a16(args):
+    """The W4A16 matmul alone at Qwen3-4B's gate+up projection shape (M = --batch or 1
+    activation rows); one JSON line."""
+    device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(device)
+    peaks = measured_peaks()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    r = w4a16_results(peaks, device, flush, shapes=(("gate_up", 2 * 9728, 2560),), ms_rows=(args.batch or 1,),
+                      iters=args.steps, warmup=args.warmup)[0]
+    line = {"metric": r["metric"], "value": r["value"], "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": r["ms"], "higher_is_better": True, "dtype": "bf16",
+            "config": {"workload": r["workload"], "l2": "flushed between launches"},
+            "roofline": {"bound": "hbm", "achieved": r["value"], "peak": peaks["hbm"], "unit": "GB/s",
+                         "frac": r["roofline_frac"], "peak_source": peaks["src"], "algorithmic_bytes": r["bytes"]}}
+    print(json.dumps(line), flush=True)
+
+
 def run_prefill(args):
     """Config 2a: dense causal prefill (flash_attention), bf16, TFLOPS of visible pairs."""
     from nano_vllm_b200 import flash_attention
@@ -674,6 +693,8 @@ def run_ours(args):
         return run_prefill(args)
     if args.config == "qkprep":
         return run_qkprep(args)
+    if args.config == "w4a16":
+        return run_w4a16(args)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -822,7 +843,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["c1", "c2a", "c3", "c4", "c5", "qkprep"], default="c3")
+    ap.add_argument("--config", choices=["c1", "c2a", "c3", "c4", "c5", "qkprep", "w4a16"], default="c3")
     ap.add_argument("--batch", type=int, default=None, help="override the config's batch (small profiling cases)")
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")

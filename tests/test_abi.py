@@ -109,3 +109,45 @@ def test_wrappers_fail_loudly_without_cuda():
         paged_attention(q, kp, kp, bt, cl, 4, mask=torch.zeros(1))
     with pytest.raises(RuntimeError, match="CUDA device"):
         flash_attention(q, kp[:1], kp[:1])
+
+
+def test_new_entry_points_validate_before_launch():
+    """Argument errors of the fused prep, the W4A16 matmul and the device page-table
+    calls come back as status codes with the operator's name, without a GPU."""
+    L = nv.lib()
+    # fused prep: fp32 inputs are refused
+    st = L.nvm_qk_norm_rope_write(None, None, None, nv.NVM_F32, 0, 0, None, None, 1e-6, None, None, 1, 0, None,
+                                  None, 0, None, None, nv.NVM_F32, None, None, nv.NVM_F16, None, 1, 1, 1, 128, 1, 16,
+                                  None)
+    assert st == -1 and L.nvm_last_error().decode().startswith("qk_norm_rope_write:")
+    # W4A16: bits and group size as the reference requires
+    assert L.nvm_w4a16_matmul(None, nv.NVM_BF16, None, None, None, None, 1, 128, 4, 128, 8, None) == -1
+    assert "bits must be 4" in L.nvm_last_error().decode()
+    assert L.nvm_w4a16_matmul(None, nv.NVM_BF16, None, None, None, None, 1, 128, 4, 64, 4, None) == -1
+    assert "group_size must be 128" in L.nvm_last_error().decode()
+    assert L.nvm_w4a16_matmul(None, nv.NVM_BF16, None, None, None, None, 1, 100, 4, 128, 4, None) == -1
+    assert "divisible by group_size" in L.nvm_last_error().decode()
+    # device page tables: batch bound
+    assert L.nvm_paged_rewind(None, None, None, None, None, None, None, None, 5000, 4, 16, 8, None) == -1
+    assert L.nvm_last_error().decode().startswith("rewind:")
+    assert L.nvm_paged_attach(None, None, None, None, None, None, 5000, 4, 16, 2, 8, None) == -1
+    assert L.nvm_last_error().decode().startswith("attach:")
+
+
+def test_new_wrappers_fail_loudly_without_cuda():
+    from nano_vllm_b200.layers.linear import quantized_matmul
+    from nano_vllm_b200.layers.qk_prep import qk_norm_rope_write
+    from nano_vllm_b200.layers.rotary_embedding import RoPE
+
+    a = torch.zeros(1, 128, dtype=torch.bfloat16)
+    b = torch.zeros(4, 16, dtype=torch.int32)
+    s = torch.ones(4, 1, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="CUDA device"):
+        quantized_matmul(s, s, 128, 4, a, b, True)
+    q = torch.zeros(1, 1, 4, 128, dtype=torch.bfloat16)
+    kv = torch.zeros(1, 1, 2, 128, dtype=torch.bfloat16)
+    w = torch.ones(128, dtype=torch.bfloat16)
+    pages = torch.zeros(1, 2, 16, 128, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="CUDA device"):
+        qk_norm_rope_write(q, kv, kv, w, w, RoPE(128, 8), torch.zeros(1, 1, dtype=torch.int32), pages, pages.clone(),
+                           torch.zeros(1, dtype=torch.int64))

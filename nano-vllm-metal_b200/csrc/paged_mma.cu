@@ -71,7 +71,11 @@ struct Cfg {
   // 16-row tile when a kv head has at most eight query rows.
   static constexpr bool kN8 = NWM == 0;
   static constexpr int kCons = (kN8 ? 1 : NWM) * NWK;
-  static constexpr int kThreads = (kCons + 1) * 32;
+  // Int8 pages on the n8 tile: no producer warp; each consumer warp refills the ring
+  // stages it consumes (stage s belongs to warp s % NWK), so a CTA is 64 threads and more
+  // CTAs fit on an SM (the kernel is latency-bound there).
+  static constexpr bool kSelfFeed = kI8 && kN8;
+  static constexpr int kThreads = (kCons + (kSelfFeed ? 0 : 1)) * 32;
   static constexpr int kRB = kN8 ? 8 : 16 * NWM;
   static constexpr int kTileBytes = 16 * D * (int)sizeof(KvT);
   // K scales at +0, V scales at +128 past the two tiles: TMA destinations are 128-byte aligned.
@@ -216,7 +220,7 @@ __global__ void __launch_bounds__(Cfg<KvT, D, NWM, NWK, NS_>::kThreads)
     else
       load_q(__nv_bfloat16{});
   }
-  if (warp == C::kCons) {
+  if (warp == (C::kSelfFeed ? 0 : C::kCons)) {
     for (int i = lane; i < n_my; i += 32) {
       const int64_t tok0 = (t_begin + i) * 16;
       const int64_t pidx = tok0 / p.ps;
@@ -226,49 +230,74 @@ __global__ void __launch_bounds__(Cfg<KvT, D, NWM, NWK, NS_>::kThreads)
   }
   __syncthreads();
 
-  // ------------------------------------------------------------------ producer
-  if (warp == C::kCons) {
-    if (lane == 0) {
-      prefetch_tmap(&tm_k);
-      prefetch_tmap(&tm_v);
+  // One ring stage's loads (tile i of the chunk into stage i % NS), by one thread.
+  auto issue_tile = [&](int i) {
+    const int s = i % NS;
+    const int pid = tile_pid[i];
+    stage_valid[s] = pid >= 0 ? 1 : 0;
+    if (pid >= 0) {
+      const int slot0 = (int)(((t_begin + i) * 16) % p.ps);
+      uint8_t* st = smem + s * C::kStageBytes;
+      mbar_arrive_expect_tx(&full[s], 2 * C::kTileBytes + (C::kI8 ? 64 : 0));
+#pragma unroll
+      for (int hb = 0; hb < C::kBoxes; ++hb) {
+        tma_load_4d(st + hb * 2048, &tm_k, hb * C::kBoxElems, slot0, (int)h, pid, &full[s]);
+        tma_load_4d(st + C::kTileBytes + hb * 2048, &tm_v, hb * C::kBoxElems, slot0, (int)h, pid, &full[s]);
+      }
       if (C::kI8) {
+        tma_load_3d(st + 2 * C::kTileBytes, &tm_ks, slot0, (int)h, pid, &full[s]);
+        tma_load_3d(st + 2 * C::kTileBytes + 128, &tm_vs, slot0, (int)h, pid, &full[s]);
+      }
+    } else {
+      mbar_arrive(&full[s]);
+    }
+  };
+
+  // ------------------------------------------------------------------ producer
+  if constexpr (!C::kSelfFeed) {
+    if (warp == C::kCons) {
+      if (lane == 0) {
+        prefetch_tmap(&tm_k);
+        prefetch_tmap(&tm_v);
+        if (C::kI8) {
+          prefetch_tmap(&tm_ks);
+          prefetch_tmap(&tm_vs);
+        }
+        int issued = 0;
+        for (int i = 0; i < n_my; ++i) {
+          const int s = i % NS;
+          if (i >= NS && !mbar_wait(&empty[s], ((i / NS) & 1) ^ 1)) {
+            record_error(p.err, kDevErrEmptyWait);
+            break;
+          }
+          issue_tile(i);
+          issued = i + 1;
+        }
+        // Drain: the last use of every stage must have landed before the CTA can exit.
+        for (int s = 0; s < NS && s < issued; ++s) {
+          const int last = s + ((issued - 1 - s) / NS) * NS;
+          if (!mbar_wait(&full[s], (last / NS) & 1)) record_error(p.err, kDevErrDrainWait);
+        }
+      }
+      return;
+    }
+  }
+  int last_issued = -1;  // self-feed: the highest tile this warp has issued (lane 0)
+  if constexpr (C::kSelfFeed) {
+    // each consumer warp fills its own first stages
+    if (lane == 0) {
+      if (warp == 0) {
+        prefetch_tmap(&tm_k);
+        prefetch_tmap(&tm_v);
         prefetch_tmap(&tm_ks);
         prefetch_tmap(&tm_vs);
       }
-      int issued = 0;
-      for (int i = 0; i < n_my; ++i) {
-        const int s = i % NS;
-        if (i >= NS && !mbar_wait(&empty[s], ((i / NS) & 1) ^ 1)) {
-          record_error(p.err, kDevErrEmptyWait);
-          break;
-        }
-        const int pid = tile_pid[i];
-        stage_valid[s] = pid >= 0 ? 1 : 0;
-        if (pid >= 0) {
-          const int slot0 = (int)(((t_begin + i) * 16) % p.ps);
-          uint8_t* st = smem + s * C::kStageBytes;
-          mbar_arrive_expect_tx(&full[s], 2 * C::kTileBytes + (C::kI8 ? 64 : 0));
-#pragma unroll
-          for (int hb = 0; hb < C::kBoxes; ++hb) {
-            tma_load_4d(st + hb * 2048, &tm_k, hb * C::kBoxElems, slot0, (int)h, pid, &full[s]);
-            tma_load_4d(st + C::kTileBytes + hb * 2048, &tm_v, hb * C::kBoxElems, slot0, (int)h, pid, &full[s]);
-          }
-          if (C::kI8) {
-            tma_load_3d(st + 2 * C::kTileBytes, &tm_ks, slot0, (int)h, pid, &full[s]);
-            tma_load_3d(st + 2 * C::kTileBytes + 128, &tm_vs, slot0, (int)h, pid, &full[s]);
-          }
-        } else {
-          mbar_arrive(&full[s]);
-        }
-        issued = i + 1;
-      }
-      // Drain: the last use of every stage must have landed before the CTA can exit.
-      for (int s = 0; s < NS && s < issued; ++s) {
-        const int last = s + ((issued - 1 - s) / NS) * NS;
-        if (!mbar_wait(&full[s], (last / NS) & 1)) record_error(p.err, kDevErrDrainWait);
+      for (int i = warp; i < n_my && i < NS; i += NWK) {
+        issue_tile(i);
+        last_issued = i;
       }
     }
-    return;
+    __syncwarp();
   }
 
   // ------------------------------------------------------------------ consumers
@@ -617,7 +646,25 @@ __global__ void __launch_bounds__(Cfg<KvT, D, NWM, NWK, NS_>::kThreads)
           }
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[(i % NS)]);
+    if constexpr (C::kSelfFeed) {
+      // the stage's shared-memory reads are done: refill it with the warp's next tile
+      if (lane == 0 && i + NS < n_my) {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        issue_tile(i + NS);
+        last_issued = i + NS;
+      }
+    } else {
+      if (lane == 0) mbar_arrive(&empty[(i % NS)]);
+    }
+  }
+  if constexpr (C::kSelfFeed) {
+    // after a timed-out wait, loads this warp issued may still be landing in its stages
+    if (timed_out && lane == 0) {
+      for (int s = wk; s < NS && s <= last_issued; s += NWK) {
+        const int last = s + ((last_issued - s) / NS) * NS;  // last tile issued into stage s
+        if (!mbar_wait(&full[s], (last / NS) & 1)) record_error(p.err, kDevErrDrainWait);
+      }
+    }
   }
   // A consumer that timed out still joins the epilogue barriers below (so no other
   // warp waits forever); its rows carry garbage and the error word is set.

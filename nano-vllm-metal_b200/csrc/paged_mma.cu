@@ -41,7 +41,8 @@ constexpr int kMaxChunkTiles = 256;
 // results never use, so one zero-filled workspace can serve calls of any shape.
 constexpr size_t kCounterBytes = 1 << 20;
 constexpr int64_t kMaxUnits = (int64_t)(kCounterBytes / sizeof(int));
-constexpr int kDefaultDecodeVariant = 3;  // c4 int8 prefers 4 (2 warps, 8 stages) by 1%
+constexpr int kDefaultDecodeVariant = 3;
+constexpr int kDefaultInt8N8Variant = 7;  // c4 int8 prefers 4 (2 warps, 8 stages) by 1%
 constexpr int kDefaultM3Variant = 1;
 
 struct MmaParams {
@@ -931,6 +932,7 @@ int launch_decode(const PagedArgs& a, const MmaPlan& plan, void* ws, cudaStream_
   switch (plan.variant) {
     case 0: return launch_cfg<KvT, ScaleT, D, NWM, 4>(a, plan, ws, s);
     case 1: return launch_cfg<KvT, ScaleT, D, NWM, 4, 12>(a, plan, ws, s);
+    case 2: return launch_cfg<KvT, ScaleT, D, NWM, 2, 2>(a, plan, ws, s);
     case 3: return launch_cfg<KvT, ScaleT, D, NWM, 2, 6>(a, plan, ws, s);
     case 4: return launch_cfg<KvT, ScaleT, D, NWM, 2, 8>(a, plan, ws, s);
     case 6: return launch_cfg<KvT, ScaleT, D, NWM, 1, 4>(a, plan, ws, s);
@@ -989,8 +991,11 @@ MmaPlan plan_paged_mma(const PagedArgs& a) {
   plan.variant = -1;
   if (plan.nwm <= 1) {
     static const int kWarps1[9] = {4, 4, 2, 2, 2, 2, 1, 2, 1};
-    plan.variant = (int)env_int("NVM_ATTN_DECODE_CFG", kDefaultDecodeVariant);
-    if (plan.variant < 0 || plan.variant > 8 || plan.variant == 2 || plan.variant == 5) plan.variant = 3;
+    // int8 pages on the n8 tile run without a producer warp: small CTAs with a short
+    // ring (2 warps x 4 stages) let the most of them share an SM
+    const int dflt = (plan.nwm == 0 && kv8) ? kDefaultInt8N8Variant : kDefaultDecodeVariant;
+    plan.variant = (int)env_int("NVM_ATTN_DECODE_CFG", dflt);
+    if (plan.variant < 0 || plan.variant > 8 || plan.variant == 5) plan.variant = 3;
     plan.nwk = kWarps1[plan.variant];
   } else if (plan.nwm == 3) {
     static const int kWarps3[4] = {2, 1, 1, 2};

@@ -10,10 +10,11 @@
 //    the g*L query rows that share kv head h (g = Hq/Hkv q heads x L tokens), packed
 //    into 16-row m-tiles, so every K/V byte is read from HBM once per kv head instead
 //    of once per q head as in the reference (grid = B*Hq there).
-//  * Keys are processed in 16-token tiles.  A producer warp streams each tile's K and
-//    V rows ([16][D] contiguous inside one page) with TMA tensor loads (128-byte
-//    swizzle, no multicast) into an NSTAGE-deep shared-memory ring guarded by
-//    mbarriers; page ids come from the block table, holes are skipped.
+//  * Keys are processed in 16-token tiles.  A producer warp (on the n8 tile, each
+//    consumer warp for the stages it consumes) streams each tile's K and V rows
+//    ([16][D] contiguous inside one page) with TMA tensor loads (128-byte swizzle, no
+//    multicast) into an NSTAGE-deep shared-memory ring guarded by mbarriers; page ids
+//    come from the block table, holes are skipped.
 //  * Consumer warps run the FA2-style online softmax on mma.sync m16n8k16 (fp32
 //    accumulate): S = Q K^T from ldmatrix'd K, P kept in registers as the A operand
 //    of O += P V with ldmatrix.trans'd V.  int8 pages are converted to f16 in
@@ -23,7 +24,7 @@
 //    separate CTAs; each writes (O, m, l) to the workspace and the last CTA of the
 //    unit (atomic ticket) merges them with log-sum-exp weights and resets the ticket.
 //  * Every mbarrier wait is bounded (nvm::mbar_wait); on expiry the kernel records an
-//    error code, the producer drains what it issued, and the CTA returns.
+//    error code, each issuing warp drains what it issued, and the CTA returns.
 #include <type_traits>
 
 #include <cstdio>
@@ -42,7 +43,7 @@ constexpr int kMaxChunkTiles = 256;
 constexpr size_t kCounterBytes = 1 << 20;
 constexpr int64_t kMaxUnits = (int64_t)(kCounterBytes / sizeof(int));
 constexpr int kDefaultDecodeVariant = 3;
-constexpr int kDefaultInt8N8Variant = 7;  // c4 int8 prefers 4 (2 warps, 8 stages) by 1%
+constexpr int kDefaultN8Variant = 7;  // c4 int8 prefers 4 (2 warps, 8 stages) by 1%
 constexpr int kDefaultM3Variant = 1;
 
 struct MmaParams {
@@ -72,10 +73,10 @@ struct Cfg {
   // 16-row tile when a kv head has at most eight query rows.
   static constexpr bool kN8 = NWM == 0;
   static constexpr int kCons = (kN8 ? 1 : NWM) * NWK;
-  // Int8 pages on the n8 tile: no producer warp; each consumer warp refills the ring
+  // The n8 tile has no producer warp: each consumer warp refills the ring
   // stages it consumes (stage s belongs to warp s % NWK), so a CTA is 64 threads and more
   // CTAs fit on an SM (the kernel is latency-bound there).
-  static constexpr bool kSelfFeed = kI8 && kN8;
+  static constexpr bool kSelfFeed = kN8;
   static constexpr int kThreads = (kCons + (kSelfFeed ? 0 : 1)) * 32;
   static constexpr int kRB = kN8 ? 8 : 16 * NWM;
   static constexpr int kTileBytes = 16 * D * (int)sizeof(KvT);
@@ -991,9 +992,9 @@ MmaPlan plan_paged_mma(const PagedArgs& a) {
   plan.variant = -1;
   if (plan.nwm <= 1) {
     static const int kWarps1[9] = {4, 4, 2, 2, 2, 2, 1, 2, 1};
-    // int8 pages on the n8 tile run without a producer warp: small CTAs with a short
-    // ring (2 warps x 4 stages) let the most of them share an SM
-    const int dflt = (plan.nwm == 0 && kv8) ? kDefaultInt8N8Variant : kDefaultDecodeVariant;
+    // the n8 tile runs without a producer warp: small CTAs with a short ring
+    // (2 warps x 4 stages) let the most of them share an SM
+    const int dflt = plan.nwm == 0 ? kDefaultN8Variant : kDefaultDecodeVariant;
     plan.variant = (int)env_int("NVM_ATTN_DECODE_CFG", dflt);
     if (plan.variant < 0 || plan.variant > 8 || plan.variant == 5) plan.variant = 3;
     plan.nwk = kWarps1[plan.variant];

@@ -1017,7 +1017,12 @@ MmaPlan plan_paged_mma(const PagedArgs& a) {
   if (dense || !can_split) {
     ct = tiles_max;  // dense callers pass no workspace: never split
   } else {
-    const int64_t target = 148 * 16;
+    // n8 tile: enough chunks for about six waves of its 8 CTAs per SM if every sequence
+    // were as long as the longest: ragged contexts leave many chunks empty, and with
+    // fewer waves the last one runs mostly idle (config 4, 64 sequences of 8K-32K keys:
+    // 160-tile chunks 4777-4807 GB/s against 4533-4564 with 256; config 3 stays at the
+    // 256 cap).  Multi-row tiles keep about 16 chunk CTAs per SM.
+    const int64_t target = plan.nwm == 0 ? 148 * 48 : 148 * 16;
     ct = (plan.n_units * tiles_max + target - 1) / target;
     ct = ((ct + 15) / 16) * 16;
     if (ct < 16) ct = 16;

@@ -256,3 +256,21 @@ def test_validation_errors(cuda):
         paged_attention(q, kp, kp, bt, cl, 16)
     with pytest.raises(RuntimeError, match="same dtype"):
         paged_attention(q[:, :2], kp, kp.float(), bt, cl, 16)
+
+
+@pytest.mark.parametrize("variant", ["2", "7", "3", "4"], ids=["ring2", "ring4", "ring6", "ring8"])
+@pytest.mark.parametrize("kvd", [torch.bfloat16, torch.int8])
+def test_n8_ring_depths_match_oracle(cuda, oracle, kvd, variant, monkeypatch):
+    """The n8 decode tile (no producer warp: each of its 2 warps refills the ring stages
+    it consumes) at every 2-warp ring depth that NVM_ATTN_DECODE_CFG can select, on
+    ragged split-K contexts with page holes and a row count that leaves the tile part empty."""
+    monkeypatch.setenv("NVM_ATTN_DECODE_CFG", variant)
+    monkeypatch.setenv("NVM_ATTN_CHUNK_TILES", "16")
+    gen = torch.Generator().manual_seed(40 + int(variant))
+    Hq, Hkv = (24, 4) if kvd == torch.int8 else (12, 4)  # 6 / 3 query rows per kv head
+    prob = random_paged_problem(gen, 7, Hq, Hkv, 1, 128, 16, kvd, 1, 1500, holes=True, empty=True)
+    for _ in range(2):
+        out = paged_attention(prob["q"], prob["kp"], prob["vp"], prob["bt"], prob["cl"], 16, prob["ks"],
+                              prob["vs"], mask="causal")
+        assert_close(out, oracle_paged(oracle, prob), TOL16)
+    assert nv.device_error(cuda) == 0

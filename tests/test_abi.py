@@ -95,6 +95,11 @@ def test_workspace_sizes():
     assert L.nvm_paged_attention_workspace_size(4, 32, 8, 2048, 128, 2048, 1, 2) == 0
     c3 = L.nvm_paged_attention_workspace_size(256, 32, 8, 1, 128, 16, 2048, 2)
     assert 0 < c3 < (1 << 30)
+    # n8 decode, 64 sequences x 8 kv heads of up to 32K keys (config 4's shape): chunks of
+    # 160 tiles (about six waves of 8 CTAs per SM), 13 per unit; tickets + (m, l) + O rows
+    units, chunks, rows, d = 64 * 8, 13, 8, 128
+    assert L.nvm_paged_attention_workspace_size(64, 64, 8, 1, d, 16, 2048, 2) == \
+        (1 << 20) + units * chunks * rows * 8 + units * chunks * rows * d * 4
     assert L.nvm_paged_attention_workspace_size(16, 16, 8, 1, 4, 4, 64, 0) == 0  # generic kernel, no workspace
 
 

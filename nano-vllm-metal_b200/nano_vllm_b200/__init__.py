@@ -2,9 +2,9 @@
 
 Drop-in for the reference's ``layers/attention`` operators and ``cache/paged``
 page pools: ``paged_attention``, ``flash_attention``, ``TinyKvPagedPool``,
-``TinyKvPagedCache``, ``PrefixCache``, ``BatchingKvCache`` keep the reference's
-names and signatures; the kernels live in ``libnvm_attn.so`` (C ABI in
-``include/nvm_attn.h``).
+``TinyKvPagedCache``, ``BatchingKvCache`` keep the reference's names and
+signatures (the reference's ``PrefixCache`` runs unchanged over these pools); the
+kernels live in ``libnvm_attn.so`` (C ABI in ``include/nvm_attn.h``).
 """
 
 from .layers.attention import (  # noqa: F401
@@ -13,11 +13,10 @@ from .layers.attention import (  # noqa: F401
     paged_attention,
     scaled_dot_product_attention_grouped,
 )
-from .cache.kv_cache import BatchingKvCache, TinyKvCache, TinyKvFullCache  # noqa: F401
+from .cache.kv_cache import BatchingKvCache, TinyKvCache  # noqa: F401
 from .cache.paged import (  # noqa: F401
     DevicePageTable,
     PagedKvMetadata,
-    PrefixCache,
     TinyKvPagedCache,
     TinyKvPagedPool,
     write_slots,

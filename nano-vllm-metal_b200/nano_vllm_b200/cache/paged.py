@@ -8,7 +8,11 @@
   becomes a view change instead of a reallocate + copy.
 * Writes go through one ``nvm_reshape_and_cache`` launch per append (all pages of
   the chunk at once), in place; int8 quantisation happens in that kernel.
-* ``PrefixCache`` (``paged.py:213-397``) is host bookkeeping over page ids.
+* The reference's ``PrefixCache`` (``paged.py:213-397``) is host bookkeeping that
+  touches a pool only through ``page_size``, ``incref``, ``free_page`` and
+  ``ref_counts`` and a request cache only through ``offset``, ``num_pages``,
+  ``page_ids`` and ``page_lens``; it runs unchanged over these classes.
+  ``DevicePageTable.attach`` is its attach step for a whole batch on the device.
 * ``TinyKvPagedCache`` (``paged.py:399-559``): per-request page list, append,
   block table, context length, rewind and release.
 * ``DevicePageTable``: batch metadata (block table, context lengths, free stack,
@@ -26,7 +30,7 @@ import torch
 from .. import _native as nv
 from .kv_cache import TinyKvCache
 
-__all__ = ["PagedKvMetadata", "TinyKvPagedPool", "PrefixCache", "TinyKvPagedCache", "DevicePageTable",
+__all__ = ["PagedKvMetadata", "TinyKvPagedPool", "TinyKvPagedCache", "DevicePageTable",
            "write_slots"]
 
 
@@ -224,124 +228,6 @@ class TinyKvPagedPool:
         base = page_id * self.page_size + start
         slots = torch.arange(base, base + S, dtype=torch.int64, device=key.device)
         self.write_slots(key, value, slots)
-
-
-class PrefixCache:
-    """Chained-hash block cache over full pages, with refcounts and LRU eviction.
-
-    Host bookkeeping only (reference ``paged.py:213-397``): entry ``pages[layer]`` is
-    a page id in ``pools[layer]``; the index holds one reference on every page it
-    stores and evicts only blocks whose pages it alone holds.
-    """
-
-    _SEED = 1469598103934665603
-
-    def __init__(self, pool, num_layers: int, max_blocks: int | None = None):
-        if isinstance(pool, (list, tuple)):
-            assert len(pool) == num_layers
-            self.pools = list(pool)
-        else:
-            self.pools = [pool] * num_layers
-        self.pool = self.pools[0]
-        self.page_size = self.pools[0].page_size
-        self.num_layers = num_layers
-        self.max_blocks = max_blocks
-        self.entries: dict[int, dict] = {}
-        self._tick = 0
-        self.evicted_blocks = 0
-
-    @property
-    def num_blocks(self) -> int:
-        return len(self.entries)
-
-    def _chain(self, parent: int, block_tokens: tuple[int, ...]) -> int:
-        return hash((parent, block_tokens))
-
-    def _touch(self, h: int) -> None:
-        self._tick += 1
-        self.entries[h]["last_used"] = self._tick
-
-    def block_hashes(self, token_ids: list[int]) -> list[tuple[int, tuple]]:
-        ps = self.page_size
-        out, parent = [], self._SEED
-        for p in range(len(token_ids) // ps):
-            block = tuple(token_ids[p * ps:(p + 1) * ps])
-            h = self._chain(parent, block)
-            out.append((h, block))
-            parent = h
-        return out
-
-    def match_prefix(self, token_ids: list[int]) -> list[int]:
-        matched, parent = [], self._SEED
-        for h, block in self.block_hashes(token_ids):
-            e = self.entries.get(h)
-            if e is None or e["tokens"] != block or e["parent"] != parent:
-                break
-            matched.append(h)
-            parent = h
-        for h in matched:
-            self._touch(h)
-        return matched
-
-    def get_pages(self, block_hash: int) -> list[int]:
-        return self.entries[block_hash]["pages"]
-
-    def attach(self, matched_hashes: list[int], caches: list["TinyKvPagedCache"]) -> int:
-        ps = self.page_size
-        assert all(c.offset == 0 and c.num_pages == 0 for c in caches), "attach expects fresh per-layer caches"
-        for h in matched_hashes:
-            pages = self.entries[h]["pages"]
-            for layer, cache in enumerate(caches):
-                pid = pages[layer]
-                self.pools[layer].incref(pid)
-                cache.page_ids.append(pid)
-                cache.page_lens.append(ps)
-        reused = len(matched_hashes) * ps
-        for cache in caches:
-            cache.offset = reused
-        return reused
-
-    def register(self, token_ids: list[int], caches: list["TinyKvPagedCache"]) -> int:
-        added, parent = 0, self._SEED
-        for p, (h, block) in enumerate(self.block_hashes(token_ids)):
-            if h not in self.entries:
-                if any(p >= c.num_pages or c.page_lens[p] != self.page_size for c in caches):
-                    break
-                pages = [caches[layer].page_ids[p] for layer in range(self.num_layers)]
-                for layer, pid in enumerate(pages):
-                    self.pools[layer].incref(pid)
-                self._tick += 1
-                self.entries[h] = {"pages": pages, "tokens": block, "parent": parent, "last_used": self._tick}
-                added += 1
-            parent = h
-        self._evict_to_capacity()
-        return added
-
-    def _is_evictable(self, entry: dict) -> bool:
-        return all(self.pools[layer].ref_counts.get(pid, 0) == 1 for layer, pid in enumerate(entry["pages"]))
-
-    def _evict_to_capacity(self) -> None:
-        if self.max_blocks is None:
-            return
-        while len(self.entries) > self.max_blocks:
-            victim, victim_used = None, None
-            for h, e in self.entries.items():
-                if not self._is_evictable(e):
-                    continue
-                if victim_used is None or e["last_used"] < victim_used:
-                    victim_used, victim = e["last_used"], h
-            if victim is None:
-                break
-            e = self.entries.pop(victim)
-            for layer, pid in enumerate(e["pages"]):
-                self.pools[layer].free_page(pid)
-            self.evicted_blocks += 1
-
-    def clear(self) -> None:
-        for e in self.entries.values():
-            for layer, pid in enumerate(e["pages"]):
-                self.pools[layer].free_page(pid)
-        self.entries.clear()
 
 
 class TinyKvPagedCache(TinyKvCache):

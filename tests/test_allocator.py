@@ -2,16 +2,64 @@
 
 Re-runs the reference's known-answer allocator tests (tests/test_paged_cache.py,
 tests/test_prefix_cache_eviction.py) on nano_vllm_b200's TinyKvPagedPool /
-TinyKvPagedCache / PrefixCache bookkeeping (``plan_append`` is the page logic of
-``_append_chunk`` without the device write), and checks it step by step against the
-oracle's restatement (oracle.PagePoolRef / PagedCacheRef) on random workloads.
+TinyKvPagedCache bookkeeping (``plan_append`` is the page logic of ``_append_chunk``
+without the device write), and checks it step by step against the oracle's
+restatement (oracle.PagePoolRef / PagedCacheRef) on random workloads.
+
+The prefix-cache tests run the REFERENCE's own ``PrefixCache`` class, loaded from the
+reference source tree, over the product pool: the drop-in claim is that the
+reference's prefix cache needs nothing but these pools.  ``mlx.core`` is replaced by
+a stub before loading (``PrefixCache`` never calls it; the module only names
+``mx.array`` in type annotations).  They are skipped where the reference tree is
+absent.
 """
 
+import importlib.util
+import os
 import random
+import sys
+import types
 
 import pytest
 
-from nano_vllm_b200 import PrefixCache, TinyKvPagedCache, TinyKvPagedPool
+from nano_vllm_b200 import TinyKvPagedCache, TinyKvPagedPool
+
+REF_PAGED = os.environ.get("NVM_REFERENCE_SRC", "/root/reference") + "/src/nano_vllm_metal/cache/paged.py"
+
+
+def _reference_prefix_cache():
+    """The reference's PrefixCache class (src/nano_vllm_metal/cache/paged.py:213-397)."""
+    if not os.path.exists(REF_PAGED):
+        pytest.skip("reference source tree not present")
+    name = "_nvm_reference_cache"
+    if name + ".paged" in sys.modules:
+        return sys.modules[name + ".paged"].PrefixCache
+    saved = {k: sys.modules.get(k) for k in ("mlx", "mlx.core")}
+    mlx = types.ModuleType("mlx")
+    core = types.ModuleType("mlx.core")
+    core.array = type("array", (), {})
+    mlx.core = core
+    pkg = types.ModuleType(name)
+    pkg.__path__ = []
+    kv = types.ModuleType(name + ".kv_cache")
+    kv.TinyKvCache = type("TinyKvCache", (), {})
+    sys.modules.update({"mlx": mlx, "mlx.core": core, name: pkg, name + ".kv_cache": kv})
+    try:
+        spec = importlib.util.spec_from_file_location(name + ".paged", REF_PAGED)
+        mod = importlib.util.module_from_spec(spec)
+        sys.modules[name + ".paged"] = mod
+        spec.loader.exec_module(mod)
+    finally:
+        for k, v in saved.items():
+            if v is None:
+                sys.modules.pop(k, None)
+            else:
+                sys.modules[k] = v
+    return mod.PrefixCache
+
+
+def PrefixCache(*args, **kwargs):  # noqa: N802 -- the reference's class, constructed over our pool
+    return _reference_prefix_cache()(*args, **kwargs)
 
 
 def test_paged_cache_page_counts():
@@ -115,7 +163,8 @@ def test_free_errors():
         TinyKvPagedPool(page_size=4, kv_bits=4)
 
 
-# --- PrefixCache (reference tests/test_prefix_cache_eviction.py:8-90) -----------
+# --- the reference's PrefixCache over the product pool
+#     (reference tests/test_prefix_cache_eviction.py:8-90) -------------------------
 
 def _run_request(pool, pc, num_layers, token_ids):
     caches = [TinyKvPagedCache(pool) for _ in range(num_layers)]

@@ -5,7 +5,7 @@ import pytest
 import torch
 
 from gpu_helpers import to_np
-from nano_vllm_b200 import BatchingKvCache, TinyKvFullCache, TinyKvPagedCache, TinyKvPagedPool, write_slots
+from nano_vllm_b200 import BatchingKvCache, TinyKvPagedCache, TinyKvPagedPool, write_slots
 
 pytestmark = pytest.mark.gpu
 
@@ -69,17 +69,18 @@ def test_int8_quantise_bit_exact(cuda, oracle, dtype):
 
 def test_paged_cache_matches_full_cache(cuda):
     gen = torch.Generator().manual_seed(3)
-    full = TinyKvFullCache()
     pool = TinyKvPagedPool(page_size=4)
     paged = TinyKvPagedCache(pool)
+    fk = fv = None  # the dense history: every chunk concatenated along the sequence
     total = 0
     for n in [3, 2, 5]:
         k = torch.randn(1, 2, n, 4, generator=gen).cuda()
         v = torch.randn(1, 2, n, 4, generator=gen).cuda()
-        fk, fv, flen, _ = full.update_and_fetch(k, v)
+        fk = k if fk is None else torch.cat([fk, k], dim=2)
+        fv = v if fv is None else torch.cat([fv, v], dim=2)
         pk, pv, plen, _ = paged.update_and_fetch(k, v)
         total += n
-        assert flen == plen == total
+        assert plen == total
         assert paged.num_pages == (total + 3) // 4
         assert [pool.read_page(p)[0].shape[2] for p in paged.page_ids] == [4] * paged.num_pages
         assert torch.equal(pk, fk) and torch.equal(pv, fv)

@@ -134,11 +134,13 @@ size_t nvm_paged_attention_workspace_size(int64_t B, int64_t Hq, int64_t Hkv, in
  * loop that cannot afford cudaMalloc's implicit device synchronisation, a host
  * without a device allocator).  Arguments and results are those of
  * nvm_paged_attention.  The split-K scratch is a 32 MiB array built into the
- * library, reserved on every GPU that loads the library until the process exits;
- * sizes whose plan needs more return NVM_ERR_WORKSPACE before any GPU work.  The
- * first call on each device resolves the array's device address (make it before
- * any stream capture).  Every call clears the scratch tickets on `stream` and
- * shares the one array: calls that overlap on the GPU race.  Allocates nothing.
+ * library; the runtime takes its device memory at the first call on each device
+ * (lazy module loading) and holds it until the process exits, so make one call, of
+ * any size, on each device before sizing page pools from the free memory and before
+ * any stream capture (that first call also resolves the array's device address).
+ * Sizes whose plan needs more than 32 MiB return NVM_ERR_WORKSPACE before any GPU
+ * work.  Every call clears the scratch tickets on `stream` and shares the one
+ * array: calls that overlap on the GPU race.  Allocates nothing.
  */
 int nvm_paged_attention_noalloc(const void* q, int q_dtype, const void* k_pages,
                                 const void* v_pages, int kv_dtype, const void* k_scales,

@@ -54,7 +54,7 @@ constexpr int64_t kSplitBelowKeys = 256;
 constexpr float kRescaleThreshold = 8.0f;  // log2(256)
 // Split-K tickets: a fixed region at the start of the workspace (one int per unit); its
 // last two ints are the work-item counter and the exit counter of the persistent grid.
-constexpr size_t kSm100CounterBytes = 1u << 20;
+constexpr size_t kSm100CounterBytes = kTicketRegionBytes;
 constexpr int64_t kMaxTicketUnits = (int64_t)(kSm100CounterBytes / sizeof(int)) - 3;
 constexpr int kPlanBins = 1024;  // tile-count bins of the plan's counting sort
 

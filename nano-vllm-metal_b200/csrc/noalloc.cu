@@ -10,13 +10,20 @@
 // the file-scope array below.
 //
 // Limits and rules:
-//  * kNoAllocScratchBytes (32 MiB) is reserved on every GPU that loads the library,
-//    for the life of the process.  A call whose split-K plan needs more returns
-//    NVM_ERR_WORKSPACE (nothing runs); use nvm_paged_attention with a workspace then.
-//  * The first call on each device looks up the array's device address with
-//    cudaGetSymbolAddress (host code cannot use the symbol itself: in host code it
-//    names a host-side stand-in, not device memory).  Make that first call before
-//    any stream capture.
+//  * kNoAllocScratchBytes (32 MiB) of device memory backs the array on each device
+//    the entry point is called on, for the life of the process.  The array is the
+//    only object of its own CUDA module, and with lazy module loading (the CUDA 12
+//    default) the runtime loads that module -- and takes the 32 MiB -- at the first
+//    call on the device, not when the library is loaded.  An engine that sizes its
+//    page pools from the free memory should therefore make one call (of any size)
+//    on each device before it does so.  A call whose split-K plan needs more than
+//    32 MiB returns NVM_ERR_WORKSPACE (nothing runs); use nvm_paged_attention with
+//    a workspace then.
+//  * Every call, whatever its size, looks up the array's device address with
+//    cudaGetSymbolAddress the first time it runs on a device (host code cannot use
+//    the symbol itself: in host code it names a host-side stand-in, not device
+//    memory), so the first call on each device does the set-up.  Make that first
+//    call before any stream capture.
 //  * All calls share the one array and it keeps the previous call's contents.  The
 //    ticket counters that must start at zero are cleared with cudaMemsetAsync on the
 //    caller's stream before every launch; calls that overlap on the GPU (different
@@ -30,8 +37,7 @@ namespace nvm {
 namespace {
 
 constexpr size_t kNoAllocScratchBytes = 32u << 20;
-// Bytes at the start of a split-K workspace that hold the tickets (see paged_mma.cu).
-constexpr size_t kTicketBytes = 1u << 20;
+static_assert(kTicketRegionBytes <= kNoAllocScratchBytes, "the ticket region must fit in the scratch array");
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
@@ -74,17 +80,19 @@ extern "C" int nvm_paged_attention_noalloc(const void* q, int q_dtype, const voi
                 "paged_attention_noalloc: these sizes need %zu bytes of split-K scratch, the built-in limit is "
                 "%zu bytes; call nvm_paged_attention with a workspace",
                 need, kNoAllocScratchBytes);
+  // resolved on every call (cached per device), so the first call of any size sets up
+  // the device and a later call that needs scratch never does it inside a capture
   void* scratch = nullptr;
+  int st = scratch_address(&scratch);
+  if (st != NVM_OK) return st;
   if (need > 0) {
-    int st = scratch_address(&scratch);
-    if (st != NVM_OK) return st;
     // the tickets must start at zero; whatever the last call left elsewhere is overwritten
-    const size_t tickets = need < kTicketBytes ? need : kTicketBytes;
+    const size_t tickets = need < kTicketRegionBytes ? need : kTicketRegionBytes;
     st = check_cuda(cudaMemsetAsync(scratch, 0, tickets, static_cast<cudaStream_t>(stream)),
                     "paged_attention_noalloc: cudaMemsetAsync");
     if (st != NVM_OK) return st;
   }
   return nvm_paged_attention(q, q_dtype, k_pages, v_pages, kv_dtype, k_scales, v_scales, scale_dtype, block_table,
                              context_lens, out, out_dtype, B, Hq, Hkv, L, D, P, page_size, max_pages, scale,
-                             is_causal, scratch, need, stream);
+                             is_causal, need > 0 ? scratch : nullptr, need, stream);
 }

@@ -20,6 +20,11 @@ int* device_error_word();
 
 size_t dtype_size(int dtype);
 
+// Bytes at the start of every split-K workspace that hold the ticket counters: zero
+// before a call, zero again after a successful one.  paged_mma.cu and flash_sm100.cu
+// lay their counters out inside this region; noalloc.cu clears exactly this much.
+constexpr size_t kTicketRegionBytes = size_t(1) << 20;
+
 // Arguments of one paged-attention call after validation.  block_table == nullptr
 // selects the dense identity layout used by flash attention: sequence b owns
 // "page" b of size page_size == S, and context_lens == nullptr means every

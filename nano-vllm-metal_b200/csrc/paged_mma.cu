@@ -40,7 +40,7 @@ namespace {
 constexpr int kMaxChunkTiles = 256;
 // Split-K tickets live in a fixed region at the start of the workspace that partial
 // results never use, so one zero-filled workspace can serve calls of any shape.
-constexpr size_t kCounterBytes = 1 << 20;
+constexpr size_t kCounterBytes = kTicketRegionBytes;
 constexpr int64_t kMaxUnits = (int64_t)(kCounterBytes / sizeof(int));
 constexpr int kDefaultDecodeVariant = 3;
 constexpr int kDefaultN8Variant = 7;  // c4 int8 prefers 4 (2 warps, 8 stages) by 1%

@@ -86,6 +86,17 @@ const char* nvm_version(void);
  */
 int nvm_device_error(void* stream, int clear);
 
+/*
+ * Failure-detection self-test (no counterpart in the reference: the reference's Metal
+ * kernels have no bounded waits).  Launches one warp on `stream` that waits on an
+ * mbarrier nobody arrives on, through the same bounded wait the kernels use, but
+ * with a limit of `limit_ns` (1e3 .. 1e8 ns) instead of 2 s.  When it expires the
+ * kernel records code 1 in the device error word and returns, so that a following
+ * nvm_device_error() returns 1 and the device keeps serving calls.  waited_ns, if
+ * not NULL, is a device uint64 that receives the time the wait took.
+ */
+int nvm_selftest_wait_expiry(int64_t limit_ns, unsigned long long* waited_ns, void* stream);
+
 /* ------------------------------------------------------------------------- */
 /* Paged attention (decode, multi-token verify, chunked prefill)              */
 /* ------------------------------------------------------------------------- */

@@ -142,16 +142,22 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Wait for the phase with `parity` to complete; false if kWaitTimeoutNs elapsed.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// Wait for the phase with `parity` to complete; false once `limit_ns` of %globaltimer
+// elapsed without it.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
 #pragma unroll 1
     for (int i = 0; i < 32; ++i)
       if (mbar_try_wait(bar, parity)) return true;
-    if (globaltimer_ns() - t0 > kWaitTimeoutNs) return false;
+    if (globaltimer_ns() - t0 > limit_ns) return false;
   }
+}
+
+// The kernels' wait: false if kWaitTimeoutNs elapsed.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  return mbar_wait_for(bar, parity, kWaitTimeoutNs);
 }
 
 __device__ __forceinline__ void record_error(int* err, int code) {

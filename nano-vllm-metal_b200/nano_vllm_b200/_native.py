@@ -36,6 +36,7 @@ SIGNATURES = {
     "nvm_last_error": (_CP, []),
     "nvm_version": (_CP, []),
     "nvm_device_error": (_I, [_P, _I]),
+    "nvm_selftest_wait_expiry": (_I, [_I64, _P, _P]),
     "nvm_paged_attention": (_I, [_P, _I, _P, _P, _I, _P, _P, _I, _P, _P, _P, _I, _I64, _I64, _I64, _I64, _I64,
                                  _I64, _I64, _I64, _F, _I, _P, _SZ, _P]),
     "nvm_paged_attention_workspace_size": (_SZ, [_I64, _I64, _I64, _I64, _I64, _I64, _I64, _I]),
@@ -117,7 +118,9 @@ def stream_ptr(device: torch.device) -> int:
 
 
 # Split-K workspace: one zero-filled buffer per (device, stream), grown on demand.
-# Kernels leave it zero-filled; calls on one stream never overlap on the GPU.
+# Successful calls leave its ticket region zero; calls on one stream never overlap on
+# the GPU.  A call whose bounded wait expired may leave tickets non-zero, so
+# device_error() re-zeroes every workspace of the device after a non-zero word.
 _workspaces: dict[tuple[int, int], torch.Tensor] = {}
 
 
@@ -133,6 +136,19 @@ def workspace(device: torch.device, nbytes: int) -> torch.Tensor | None:
 
 
 def device_error(device: torch.device, clear: bool = True) -> int:
-    """Synchronise and read the device error word (0 = no bounded wait expired)."""
+    """Synchronise and read the device error word (0 = no bounded wait expired).
+
+    After a non-zero word (a kernel gave up on a wait and returned early), the split-K
+    workspaces cached for this device are zero-filled again once the device is idle,
+    so the next call cannot merge a half-finished call's tickets or partials.
+    """
     with torch.cuda.device(device):
-        return int(lib().nvm_device_error(stream_ptr(device), 1 if clear else 0))
+        word = int(lib().nvm_device_error(stream_ptr(device), 1 if clear else 0))
+        if word != 0:
+            index = device.index if device.index is not None else torch.cuda.current_device()
+            torch.cuda.synchronize(device)
+            for (dev_index, _), ws in _workspaces.items():
+                if dev_index == index:
+                    ws.zero_()
+            torch.cuda.synchronize(device)
+        return word

@@ -156,3 +156,10 @@ def test_new_wrappers_fail_loudly_without_cuda():
     with pytest.raises(RuntimeError, match="CUDA device"):
         qk_norm_rope_write(q, kv, kv, w, w, RoPE(128, 8), torch.zeros(1, 1, dtype=torch.int32), pages, pages.clone(),
                            torch.zeros(1, dtype=torch.int64))
+
+
+def test_selftest_limit_validated_before_any_device_work():
+    L = nv.lib()
+    for bad in (0, 999, 100_000_001):
+        assert L.nvm_selftest_wait_expiry(bad, None, None) == -1
+        assert L.nvm_last_error().decode().startswith("selftest_wait_expiry: limit")

@@ -32,6 +32,7 @@
  *   src/nano_vllm_metal/models/qwen3.py:100-116            (q/k norm, RoPE, cache update)
  *   src/nano_vllm_metal/layers/layernorm.py:4-14, layers/rotary_embedding.py:74-124
  *   src/nano_vllm_metal/metal/src/quantized_matmul.cpp:7-270  (W4A16 matmul)
+ *   src/nano_vllm_metal/engine/generate.py:130-169         (speculative acceptance)
  */
 #ifndef NVM_ATTN_H_
 #define NVM_ATTN_H_
@@ -303,6 +304,32 @@ int nvm_paged_attach(int32_t* block_table, int32_t* context_lens, const int32_t*
                      const int32_t* count, int32_t* page_refcount, int32_t* status, int64_t B,
                      int64_t max_pages, int64_t page_size, int64_t max_prefix, int64_t capacity,
                      void* stream);
+
+/*
+ * Batched speculative-decoding acceptance on the device.  Replaces, for a whole batch
+ * in one launch, the per-request acceptance loop of speculative_generate
+ * (src/nano_vllm_metal/engine/generate.py:130-169), whose result drives the rewind of
+ * cache/paged.py:530-550 (nvm_paged_rewind here).
+ *
+ * candidates [B, K1] int32: the request's last accepted token, then its K1 - 1 drafts.
+ * verified   [B, K1] int32: the target model's argmax at each of the K1 positions.
+ * Request b walks positions i = 0 .. K1-1, comparing (i == 0 ? candidates[b][0] :
+ * verified[b][i-1]) with candidates[b][i]:
+ *   match: the token is emitted, unless it equals eos_id (request finished, token not
+ *     emitted); when budget[b] >= 0 tokens have been emitted the request is finished;
+ *   first mismatch at i: rewind[b] = K1 - i tokens are dropped from the target cache,
+ *     draft_rewind[b] = K1 - i - 1 from the draft cache, next_token[b] =
+ *     verified[b][i-1] (finished if it equals eos_id);
+ *   all matched: next_token[b] = verified[b][K1-1], rewind[b] = draft_rewind[b] = 0.
+ * Outputs: emitted [B, K1] (-1 padded), n_emitted, next_token (-1 when finished by an
+ * emitted eos or the budget), rewind, draft_rewind, finished (0/1), all [B] int32.
+ * budget and active ([B] int32, active[b] == 0 marks an idle slot with zero outputs)
+ * may be NULL; eos_id < 0 disables the end-of-sequence check.
+ */
+int nvm_spec_verify_accept(const int32_t* candidates, const int32_t* verified, int64_t B, int64_t K1,
+                           int32_t eos_id, const int32_t* budget, const int32_t* active,
+                           int32_t* emitted, int32_t* n_emitted, int32_t* next_token, int32_t* rewind,
+                           int32_t* draft_rewind, int32_t* finished, void* stream);
 
 /* ------------------------------------------------------------------------- */
 /* W4A16 quantized matmul (4-bit weights, group 128)                          */

@@ -1,6 +1,6 @@
 // nvm_common.cuh -- device helpers shared by the sm_100a kernels of libnvm_attn.so:
-// element conversion, mbarrier with bounded waits, TMA tensor loads (no multicast
-// anywhere in this library), ldmatrix / mma.sync fragments, and the launch-side
+// element conversion, mbarrier with bounded waits, TMA tensor loads (plain tile mode,
+// each CTA loading into its own shared memory), ldmatrix / mma.sync fragments, and the launch-side
 // parameter structs.
 #pragma once
 
@@ -171,7 +171,7 @@ __device__ __forceinline__ void named_barrier(int id, int nthreads) {
 
 // ---------------------------------------------------------------------------
 // TMA (tensor) loads into this CTA's shared memory, completing on an mbarrier.
-// Plain tile mode; multicast is never used by this library.
+// Plain tile mode only: every load fills the issuing CTA's own shared memory.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int c0, int c1, int c2,
                                             uint64_t* bar) {

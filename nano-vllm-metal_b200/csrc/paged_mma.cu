@@ -12,8 +12,8 @@
 //    of once per q head as in the reference (grid = B*Hq there).
 //  * Keys are processed in 16-token tiles.  A producer warp (on the n8 tile, each
 //    consumer warp for the stages it consumes) streams each tile's K and V rows
-//    ([16][D] contiguous inside one page) with TMA tensor loads (128-byte swizzle, no
-//    multicast) into an NSTAGE-deep shared-memory ring guarded by mbarriers; page ids
+//    ([16][D] contiguous inside one page) with plain tile-mode TMA tensor loads
+//    (128-byte swizzle) into an NSTAGE-deep shared-memory ring guarded by mbarriers; page ids
 //    come from the block table, holes are skipped.
 //  * Consumer warps run the FA2-style online softmax on mma.sync m16n8k16 (fp32
 //    accumulate): S = Q K^T from ldmatrix'd K, P kept in registers as the A operand

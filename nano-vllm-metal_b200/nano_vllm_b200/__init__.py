@@ -21,6 +21,7 @@ from .cache.paged import (  # noqa: F401
     TinyKvPagedPool,
     write_slots,
 )
+from .spec_verify import VerifyResult, verify_accept  # noqa: F401
 from . import _native  # noqa: F401
 
 __version__ = "0.1.0"

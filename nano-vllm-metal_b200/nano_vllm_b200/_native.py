@@ -49,6 +49,7 @@ SIGNATURES = {
     "nvm_paged_append": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _I64, _P, _I64, _I64, _I64, _I64, _P]),
     "nvm_paged_rewind": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P]),
     "nvm_paged_attach": (_I, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P]),
+    "nvm_spec_verify_accept": (_I, [_P, _P, _I64, _I64, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "nvm_w4a16_matmul": (_I, [_P, _I, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P]),
     "nvm_qk_norm_rope_write": (_I, [_P, _P, _P, _I, _I64, _I64, _P, _P, _F, _P, _P, _I64, _I, _P, _P, _I64, _P,
                                     _P, _I, _P, _P, _I, _P, _I64, _I64, _I64, _I64, _I64, _I64, _P]),

@@ -413,6 +413,15 @@ class DevicePageTable:
             n = torch.where(mask.to(device=self.device, dtype=torch.bool), n, torch.zeros_like(n))
         self.rewind(n)
 
+    def apply_verify(self, result) -> None:
+        """After a batched speculative verify step (``spec_verify.verify_accept``): drop
+        each request's rejected suffix (``result.rewind``) and release the requests that
+        finished, in one batched rewind on the device -- the reference's per-request
+        ``rewind`` (``engine/generate.py:147-153``, ``paged.py:530-550``) and the release
+        of finished requests."""
+        fin = result.finished.to(device=self.device, dtype=torch.bool)
+        self.rewind(torch.where(fin, self.context_lens, result.rewind.to(device=self.device, dtype=torch.int32)))
+
     def attach(self, pages: torch.Tensor, count: torch.Tensor) -> None:
         """``PrefixCache.attach`` on the device (``paged.py:305-328``): fresh request b
         takes the shared full pages ``pages[b, :count[b]]`` (each gains a reference) and

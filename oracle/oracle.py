@@ -16,7 +16,9 @@ plain Python the pieces of the reference that are Python-level:
   (q_norm / k_norm, RoPE of ``layers/rotary_embedding.py:74-124``, the paged write
   of K and V), with ``rope_tables_ref`` restating ``rotary_embedding.py:28-44``,
 * ``PagePoolRef`` / ``PagedCacheRef`` -- the allocator and append bookkeeping of
-  ``paged.py:60-75,197-210,424-459,491-559`` (page ids, page_lens, rewind).
+  ``paged.py:60-75,197-210,424-459,491-559`` (page ids, page_lens, rewind),
+* ``spec_accept_ref`` -- the per-request acceptance loop of speculative decoding,
+  ``src/nano_vllm_metal/engine/generate.py:130-169``.
 
 The reference itself cannot run here (MLX / Metal only) and publishes no golden
 vectors; parity is pinned by re-running its own differential tests and
@@ -359,6 +361,32 @@ def quantize_w4_ref(w: np.ndarray, group_size: int = 128):
     for j in range(8):
         packed |= q[:, j::8] << np.uint32(4 * j)
     return packed, scale, lo.astype(np.float32)
+
+
+# ---------------------------------------------------------------------------
+# speculative-decoding acceptance (pure Python)
+# ---------------------------------------------------------------------------
+
+def spec_accept_ref(candidates, verified, eos_id=None, budget=None):
+    """The acceptance loop of speculative_generate (engine/generate.py:130-169) for one
+    request: candidates = [last token, drafts...], verified = the target's argmax at
+    each position.  Returns (emitted tokens, next token or None, target rewind, draft
+    rewind, finished).  budget = tokens the request may still emit (None = unlimited),
+    standing for the reference's max_tokens check after every emitted token."""
+    k1 = len(candidates)
+    comparable = [candidates[0]] + list(verified[:-1])
+    emitted = []
+    for i in range(k1):
+        if comparable[i] != candidates[i]:
+            rejected = k1 - i  # generate.py:145-153
+            nxt = comparable[i]
+            return emitted, nxt, rejected, rejected - 1, eos_id is not None and nxt == eos_id
+        if eos_id is not None and comparable[i] == eos_id:  # _decode_one returns False
+            return emitted, None, 0, 0, True
+        emitted.append(comparable[i])
+        if budget is not None and len(emitted) >= budget:  # max_tokens reached
+            return emitted, None, 0, 0, True
+    return emitted, verified[-1], 0, 0, False
 
 
 # ---------------------------------------------------------------------------

@@ -1109,6 +1109,7 @@ def run_ours(args):
         # NCCL's init log (one line per rank and channel setup) shows the ranks it joined
         os.environ.setdefault("NCCL_DEBUG", "INFO")
         os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")  # keep stdout for the JSON line
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
     peaks = measured_peaks()
     cfg = decode_config(args.config)

@@ -80,7 +80,9 @@ struct MmaPlan {
   int64_t chunk_tiles;    // 16-token tiles per CTA (split-K granularity)
   int64_t n_chunks;       // max chunks per unit
   int64_t n_units;
-  size_t ws_bytes;        // workspace for the split-K combine (0 if n_chunks == 1)
+  size_t ws_bytes;        // workspace for the split-K combine (0 if n_chunks == 1 or cluster)
+  int cluster;            // 1: a unit's n_chunks CTAs form one thread-block cluster and merge
+                          // their partial results over distributed shared memory (no workspace)
 };
 MmaPlan plan_paged_mma(const PagedArgs& a);
 int launch_paged_mma(const PagedArgs& a, const MmaPlan& plan, void* workspace, cudaStream_t s);

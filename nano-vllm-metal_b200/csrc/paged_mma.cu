@@ -25,6 +25,7 @@
 //    unit (atomic ticket) merges them with log-sum-exp weights and resets the ticket.
 //  * Every mbarrier wait is bounded (nvm::mbar_wait); on expiry the kernel records an
 //    error code, each issuing warp drains what it issued, and the CTA returns.
+#include <cooperative_groups.h>
 #include <type_traits>
 
 #include <cstdio>
@@ -61,6 +62,7 @@ struct MmaParams {
   int64_t n_rb, rows_real, ct, n_chunks;
   float scale_log2;   // softmax scale * log2(e)
   int causal;
+  int cluster;        // the n_chunks CTAs of a unit are one cluster: merge over DSMEM
 };
 
 template <typename KvT, int D, int NWM, int NWK, int NS_ = 0>
@@ -89,6 +91,11 @@ struct Cfg {
   static constexpr int kEpiBytes = NWK * kRB * D * 4 + 2 * NWK * kRB * 4;
   static constexpr int kRingBytes = kStages * kStageBytes;
   static constexpr int kMainBytes = kRingBytes > kEpiBytes ? kRingBytes : kEpiBytes;
+  // cluster merge (n8 tile): this CTA's combined partial rows [kRB][D], their (m, l) and
+  // the chunk weights [8][kRB] + sums [kRB], placed after the epilogue staging area
+  static constexpr int kClusterOff = ((kEpiBytes + 15) / 16) * 16;
+  static constexpr int kClusterBytes = kRB * D * 4 + kRB * 8 + 8 * kRB * 4 + kRB * 4;
+  static constexpr bool kClusterFits = kN8 && kClusterOff + kClusterBytes <= kMainBytes;
   static constexpr int kSmemBytes = 1024 + kMainBytes + kStages * 16 + kStages * 4 + kMaxChunkTiles * 4 + 16;
   static_assert(kStages % NWK == 0, "stage ring must be a multiple of the k-split");
   static_assert(D % 64 == 0, "head dim must be 64 or 128");
@@ -152,21 +159,7 @@ __global__ void __launch_bounds__(Cfg<KvT, D, NWM, NWK, NS_>::kThreads)
   const int64_t ctx_limit = ctx < cap ? ctx : cap;
   const int64_t row0 = rb * C::kRB;
   const int64_t rows_here = (p.M - row0) < C::kRB ? (p.M - row0) : C::kRB;
-  int64_t need_keys = ctx_limit;
-  if (p.causal) {
-    const bool spans = rows_here >= p.L || (row0 % p.L) + rows_here > p.L;
-    const int64_t lmax = spans ? p.L - 1 : (row0 + rows_here - 1) % p.L;
-    const int64_t lim = lmax + ctx - p.L + 1;
-    if (lim < need_keys) need_keys = lim;
-  }
-  if (ctx <= 0 || need_keys < 0) need_keys = 0;
-  const int64_t n_tiles = (need_keys + 15) / 16;
-  const int64_t n_chunks = n_tiles > 0 ? (n_tiles + p.ct - 1) / p.ct : 1;
-  if (c >= n_chunks) return;
   const int64_t t_begin = c * p.ct;
-  int64_t n_left = n_tiles - t_begin;
-  if (n_left > p.ct) n_left = p.ct;
-  const int n_my = n_left > 0 ? (int)n_left : 0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < NS; ++s) {
@@ -223,14 +216,43 @@ __global__ void __launch_bounds__(Cfg<KvT, D, NWM, NWK, NS_>::kThreads)
       load_q(__nv_bfloat16{});
   }
   if (warp == (C::kSelfFeed ? 0 : C::kCons)) {
-    for (int i = lane; i < n_my; i += 32) {
-      const int64_t tok0 = (t_begin + i) * 16;
-      const int64_t pidx = tok0 / p.ps;
-      const int64_t pid = p.block_table ? (int64_t)p.block_table[b * p.mp + pidx] : b;
-      tile_pid[i] = (pid >= 0 && pid < p.P) ? (int)pid : -1;
+    // The chunk's block-table entries, read together with (not after) the context
+    // length: the row holds mp entries, so entries past the context are in bounds and
+    // simply never used.  All loads are issued before any is consumed.
+    int64_t n_tab = (cap + 15) / 16 - t_begin;
+    if (n_tab > p.ct) n_tab = p.ct;
+    constexpr int kPer = kMaxChunkTiles / 32;
+    int64_t pv[kPer];
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int i = lane + 32 * j;
+      pv[j] = -1;
+      if (i < n_tab) pv[j] = p.block_table ? (int64_t)__ldg(&p.block_table[b * p.mp + ((t_begin + i) * 16) / p.ps]) : b;
+    }
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int i = lane + 32 * j;
+      if (i < n_tab) tile_pid[i] = (pv[j] >= 0 && pv[j] < p.P) ? (int)pv[j] : -1;
     }
   }
   __syncthreads();
+
+  int64_t need_keys = ctx_limit;
+  if (p.causal) {
+    const bool spans = rows_here >= p.L || (row0 % p.L) + rows_here > p.L;
+    const int64_t lmax = spans ? p.L - 1 : (row0 + rows_here - 1) % p.L;
+    const int64_t lim = lmax + ctx - p.L + 1;
+    if (lim < need_keys) need_keys = lim;
+  }
+  if (ctx <= 0 || need_keys < 0) need_keys = 0;
+  const int64_t n_tiles = (need_keys + 15) / 16;
+  const int64_t n_chunks = n_tiles > 0 ? (n_tiles + p.ct - 1) / p.ct : 1;
+  // A chunk past this unit's keys has nothing to do; inside a cluster it still takes
+  // part in the cluster barriers of the merge (with no tiles), so it does not return.
+  if (c >= n_chunks && !(C::kClusterFits && p.cluster)) return;
+  int64_t n_left = n_tiles - t_begin;
+  if (n_left > p.ct) n_left = p.ct;
+  const int n_my = n_left > 0 ? (int)n_left : 0;
 
   // One ring stage's loads (tile i of the chunk into stage i % NS), by one thread.
   auto issue_tile = [&](int i) {
@@ -342,10 +364,13 @@ __global__ void __launch_bounds__(Cfg<KvT, D, NWM, NWK, NS_>::kThreads)
       const int64_t tok0 = (t_begin + i) * 16;
       const uint32_t kt = smem_u32(smem + s * C::kStageBytes);
       const uint32_t vt = kt + C::kTileBytes;
-      // S^T = K Q^T (16 keys x 8 rows); even / odd k-steps in two accumulator chains
-      float sacc[2][4];
+      // S^T = K Q^T (16 keys x 8 rows).  16-bit pages: the k-steps go round-robin into
+      // four independent accumulator chains (the mma.sync result latency, not issue,
+      // bounds a warp walking its tiles); int8 pages (issue-bound): two chains.
+      constexpr int kQc = C::kI8 ? 2 : 4;
+      float sacc[kQc][4];
 #pragma unroll
-      for (int q2 = 0; q2 < 2; ++q2) sacc[q2][0] = sacc[q2][1] = sacc[q2][2] = sacc[q2][3] = 0.f;
+      for (int q2 = 0; q2 < kQc; ++q2) sacc[q2][0] = sacc[q2][1] = sacc[q2][2] = sacc[q2][3] = 0.f;
       if constexpr (!C::kI8) {
         const int mi = lane >> 3;
         const int ktok = (mi >> 1) * 8 + (lane & 7);
@@ -354,7 +379,7 @@ __global__ void __launch_bounds__(Cfg<KvT, D, NWM, NWK, NS_>::kThreads)
           uint32_t k0, k1, k2, k3;
           ldsm_x4(swz(kt, ktok, 2 * ks + (mi & 1)), k0, k1, k2, k3);
           const uint32_t a[4] = {k0, k2, k1, k3};
-          mma16816<MmaT>(sacc[ks & 1], a, qa[ks][0], qa[ks][2]);
+          mma16816<MmaT>(sacc[ks % kQc], a, qa[ks][0], qa[ks][2]);
         }
       } else {
         // keys r and r + 8, bytes [32 cq, 32 cq + 32) of each (the k dimension is
@@ -388,7 +413,12 @@ __global__ void __launch_bounds__(Cfg<KvT, D, NWM, NWK, NS_>::kThreads)
       // sv[0] = (key r, row 2cq), [1] = (key r, row 2cq+1), [2] = (key r+8, row 2cq), [3] = (key r+8, row 2cq+1)
       float sv[4];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) sv[e] = sacc[0][e] + sacc[1][e];
+      for (int e = 0; e < 4; ++e) {
+        if constexpr (kQc == 4)
+          sv[e] = (sacc[0][e] + sacc[1][e]) + (sacc[2][e] + sacc[3][e]);
+        else
+          sv[e] = sacc[0][e] + sacc[1][e];
+      }
       const bool need_mask = tok0 + 16 > clean;
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
@@ -729,6 +759,80 @@ __global__ void __launch_bounds__(Cfg<KvT, D, NWM, NWK, NS_>::kThreads)
   }
   named_barrier(1, NCT);
   const int tid = threadIdx.x;
+  if constexpr (C::kClusterFits) {
+    if (p.cluster) {
+      // Split-K inside a thread-block cluster: the unit's chunks are CTAs 0 .. n_chunks-1
+      // of one cluster (cluster rank == chunk index).  Each leaves its combined partial
+      // rows (O, m, l) in its own shared memory; chunk 0 merges them over distributed
+      // shared memory with the same operations, in the same chunk order, as the
+      // workspace merge below.  Every CTA of the cluster, with or without keys, reaches
+      // both cluster barriers; the second one keeps the partials alive until read.
+      namespace cg = cooperative_groups;
+      cg::cluster_group cluster = cg::this_cluster();
+      float* cb_o = reinterpret_cast<float*>(smem + C::kClusterOff);  // [kRB][D]
+      float2* cb_ml = reinterpret_cast<float2*>(cb_o + C::kRB * D);   // [kRB]
+      float* cw = reinterpret_cast<float*>(cb_ml + C::kRB);           // [8][kRB] chunk weights
+      float* cwl = cw + 8 * C::kRB;                                   // [kRB]
+      for (int64_t idx = tid; idx < rows_here * D; idx += NCT) {
+        const int rl = (int)(idx / D), d = (int)(idx % D);
+        float ms = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < NWK; ++w) ms = fmaxf(ms, em[w * C::kRB + rl]);
+        float ls = 0.f, os = 0.f;
+#pragma unroll
+        for (int w = 0; w < NWK; ++w) {
+          const float mw = em[w * C::kRB + rl];
+          if (mw != -INFINITY) {
+            const float f = exp2f(mw - ms);
+            ls += el[w * C::kRB + rl] * f;
+            os += eo[(w * C::kRB + rl) * D + d] * f;
+          }
+        }
+        cb_o[rl * D + d] = os;
+        if (d == 0) cb_ml[rl] = make_float2(ms, ls);
+      }
+      cluster.sync();
+      if (c == 0) {
+        const int nc = (int)n_chunks;  // chunks of this unit that hold keys (<= cluster size)
+        for (int rl = tid; rl < rows_here; rl += NCT) {
+          float ms = -INFINITY;
+          for (int cc = 0; cc < nc; ++cc) ms = fmaxf(ms, cluster.map_shared_rank(cb_ml, cc)[rl].x);
+          float ls = 0.f;
+          for (int cc = 0; cc < nc; ++cc) {
+            const float2 ml = cluster.map_shared_rank(cb_ml, cc)[rl];
+            float f = -1.f;
+            if (ml.x != -INFINITY) {
+              f = exp2f(ml.x - ms);
+              ls += ml.y * f;
+            }
+            cw[cc * C::kRB + rl] = f;
+          }
+          cwl[rl] = ls;
+        }
+        named_barrier(1, NCT);
+        for (int64_t g4 = tid; g4 < rows_here * (D / 4); g4 += NCT) {
+          const int rl = (int)(g4 / (D / 4)), d = (int)(g4 % (D / 4)) * 4;
+          float o4[4] = {0.f, 0.f, 0.f, 0.f};
+          for (int cc = 0; cc < nc; ++cc) {
+            const float f = cw[cc * C::kRB + rl];
+            if (f >= 0.f) {
+              const float4 v = *reinterpret_cast<const float4*>(cluster.map_shared_rank(cb_o + rl * D + d, cc));
+              o4[0] += v.x * f;
+              o4[1] += v.y * f;
+              o4[2] += v.z * f;
+              o4[3] += v.w * f;
+            }
+          }
+          const float ls = cwl[rl];
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            store_dyn(p.out, (q_row0 + row0 + rl) * D + d + e, p.out_dtype, ls > 0.f ? o4[e] / ls : 0.f);
+        }
+      }
+      cluster.sync();
+      return;
+    }
+  }
   const bool single = n_chunks == 1;
   const int64_t wsrow = (unit * p.n_chunks + c) * p.rows_real;
   for (int64_t idx = tid; idx < rows_here * D; idx += NCT) {
@@ -917,7 +1021,26 @@ int launch_cfg(const PagedArgs& a, const MmaPlan& plan, void* ws, cudaStream_t s
   p.n_rb = plan.n_row_blocks; p.rows_real = plan.rows_real; p.ct = plan.chunk_tiles; p.n_chunks = plan.n_chunks;
   p.scale_log2 = a.scale * 1.4426950408889634f;
   p.causal = a.is_causal;
+  p.cluster = 0;
   const dim3 grid((unsigned)plan.n_units, (unsigned)plan.n_chunks);
+  if (plan.cluster && C::kClusterFits && plan.n_chunks > 1 && plan.n_chunks <= 8) {
+    p.cluster = 1;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(C::kThreads, 1, 1);
+    cfg.dynamicSmemBytes = C::kSmemBytes;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = (unsigned)plan.n_chunks;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return check_cuda(cudaLaunchKernelEx(&cfg, kern, tk, tv, tks, tvs, p),
+                      "paged_attention: tensor-core kernel launch (cluster)");
+  }
+  if (plan.cluster) return fail(NVM_ERR_UNSUPPORTED, "paged_attention: cluster plan for a kernel without it");
   kern<<<grid, C::kThreads, C::kSmemBytes, s>>>(tk, tv, tks, tvs, p);
   return check_cuda(cudaGetLastError(), "paged_attention: tensor-core kernel launch");
 }
@@ -1037,6 +1160,20 @@ MmaPlan plan_paged_mma(const PagedArgs& a) {
   plan.n_chunks = (tiles_max + ct - 1) / ct;
   if (plan.n_chunks < 1) plan.n_chunks = 1;
   if (plan.n_chunks > 65535) return plan;
+  // n8 tile with 2..8 chunks: the chunks of a unit merge inside a thread-block cluster
+  // (distributed shared memory) instead of through the workspace, which takes the
+  // global-memory round trips of the split-K merge off every unit's critical path.
+  // Every CTA of a cluster stays resident until its unit is merged, so chunks without
+  // keys (ragged contexts) idle in their slots; the cluster merge is therefore used
+  // when the launch fits in one wave (about six n8 CTAs per SM) or a unit has at most
+  // four chunks.
+  // NVM_ATTN_CLUSTER: 0 never, 2 whenever 2..8 chunks (sweeps), otherwise the rule above.
+  plan.cluster = 0;
+  const int64_t cl_mode = env_int("NVM_ATTN_CLUSTER", 1);
+  if (plan.nwm == 0 && !dense && can_split && plan.n_chunks >= 2 && plan.n_chunks <= 8 && cl_mode != 0) {
+    const bool one_wave = plan.n_units * plan.n_chunks <= 148 * 6;
+    if (cl_mode == 2 || one_wave || plan.n_chunks <= 4) plan.cluster = 1;
+  }
   if (dense && ct > kMaxChunkTiles) {
     // The per-CTA page table holds kMaxChunkTiles entries; a dense sequence longer
     // than that is still one page, so only its first entry is read -- but keep the
@@ -1045,7 +1182,7 @@ MmaPlan plan_paged_mma(const PagedArgs& a) {
     return plan;
   }
   plan.ws_bytes = 0;
-  if (plan.n_chunks > 1) {
+  if (plan.n_chunks > 1 && !plan.cluster) {
     plan.ws_bytes = kCounterBytes + align256(plan.n_units * plan.n_chunks * plan.rows_real * sizeof(float2)) +
                     (size_t)plan.n_units * plan.n_chunks * plan.rows_real * a.D * sizeof(float);
   }

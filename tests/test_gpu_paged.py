@@ -161,6 +161,26 @@ def test_split_k_combine(cuda, oracle, kvd, monkeypatch):
     assert nv.device_error(cuda) == 0
 
 
+@pytest.mark.parametrize("kvd", [torch.float16, torch.bfloat16, torch.int8])
+@pytest.mark.parametrize("chunk_tiles", ["8", "16", "32"])
+def test_cluster_merge_equals_workspace_merge(cuda, oracle, kvd, chunk_tiles, monkeypatch):
+    """n8 decode split into 2..8 chunks: merged inside a thread-block cluster over
+    distributed shared memory, or through the workspace -- the same operations in the
+    same order, so bit-identical -- and both equal the oracle.  Ragged contexts (chunks
+    without keys still join the cluster), holes, an empty sequence."""
+    monkeypatch.setenv("NVM_ATTN_CHUNK_TILES", chunk_tiles)
+    gen = torch.Generator().manual_seed(int(chunk_tiles) + 7)
+    prob = random_paged_problem(gen, 9, 16, 8, 1, 128, 16, kvd, 1, 1024, holes=True, empty=True)
+    args = (prob["q"], prob["kp"], prob["vp"], prob["bt"], prob["cl"], 16, prob["ks"], prob["vs"])
+    outs = {}
+    for mode in ("0", "2"):
+        monkeypatch.setenv("NVM_ATTN_CLUSTER", mode)
+        outs[mode] = [paged_attention(*args, mask="causal") for _ in range(2)]
+    assert torch.equal(outs["0"][0], outs["2"][0]) and torch.equal(outs["2"][0], outs["2"][1])
+    assert_close(outs["2"][0], oracle_paged(oracle, prob), TOL16)
+    assert nv.device_error(cuda) == 0
+
+
 def test_workspace_shared_across_shapes(cuda, oracle):
     """One cached workspace serves split-K calls of different shapes back to back."""
     gen = torch.Generator().manual_seed(21)

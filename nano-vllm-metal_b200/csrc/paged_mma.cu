@@ -90,12 +90,14 @@ struct Cfg {
   static constexpr int kBoxes = D / kBoxElems;
   static constexpr int kEpiBytes = NWK * kRB * D * 4 + 2 * NWK * kRB * 4;
   static constexpr int kRingBytes = kStages * kStageBytes;
-  static constexpr int kMainBytes = kRingBytes > kEpiBytes ? kRingBytes : kEpiBytes;
   // cluster merge (n8 tile): this CTA's combined partial rows [kRB][D], their (m, l) and
   // the chunk weights [8][kRB] + sums [kRB], placed after the epilogue staging area
   static constexpr int kClusterOff = ((kEpiBytes + 15) / 16) * 16;
   static constexpr int kClusterBytes = kRB * D * 4 + kRB * 8 + 8 * kRB * 4 + kRB * 4;
-  static constexpr bool kClusterFits = kN8 && kClusterOff + kClusterBytes <= kMainBytes;
+  // only self-feeding CTAs (every warp is a consumer and reaches the cluster barriers)
+  static constexpr bool kClusterFits = kN8 && kSelfFeed;
+  static constexpr int kEpiAll = kClusterFits ? kClusterOff + kClusterBytes : kEpiBytes;
+  static constexpr int kMainBytes = kRingBytes > kEpiAll ? kRingBytes : kEpiAll;
   static constexpr int kSmemBytes = 1024 + kMainBytes + kStages * 16 + kStages * 4 + kMaxChunkTiles * 4 + 16;
   static_assert(kStages % NWK == 0, "stage ring must be a multiple of the k-split");
   static_assert(D % 64 == 0, "head dim must be 64 or 128");
@@ -1116,7 +1118,9 @@ MmaPlan plan_paged_mma(const PagedArgs& a) {
   if (plan.nwm <= 1) {
     static const int kWarps1[9] = {4, 4, 2, 2, 2, 2, 1, 2, 1};
     // the n8 tile runs without a producer warp: small CTAs with a short ring
-    // (2 warps x 4 stages) let the most of them share an SM
+    // (2 warps x 4 stages) let the most of them share an SM (one CTA per unit with a
+    // producer and 12 consumer warps measured 1.9x slower on config 1: a unit's pages
+    // have to come through many SMs)
     const int dflt = plan.nwm == 0 ? kDefaultN8Variant : kDefaultDecodeVariant;
     plan.variant = (int)env_int("NVM_ATTN_DECODE_CFG", dflt);
     if (plan.variant < 0 || plan.variant > 8 || plan.variant == 5) plan.variant = 3;
@@ -1170,7 +1174,8 @@ MmaPlan plan_paged_mma(const PagedArgs& a) {
   // NVM_ATTN_CLUSTER: 0 never, 2 whenever 2..8 chunks (sweeps), otherwise the rule above.
   plan.cluster = 0;
   const int64_t cl_mode = env_int("NVM_ATTN_CLUSTER", 1);
-  if (plan.nwm == 0 && !dense && can_split && plan.n_chunks >= 2 && plan.n_chunks <= 8 && cl_mode != 0) {
+  if (plan.nwm == 0 && plan.nwk <= 4 && !dense && can_split && plan.n_chunks >= 2 && plan.n_chunks <= 8 &&
+      cl_mode != 0) {
     const bool one_wave = plan.n_units * plan.n_chunks <= 148 * 6;
     if (cl_mode == 2 || one_wave || plan.n_chunks <= 4) plan.cluster = 1;
   }

@@ -1088,11 +1088,49 @@ def run_prefill(args):
           flush=True)
 
 
+def run_chunked(args):
+    """Config 2b alone: 4 x 512 new tokens against --prior paged tokens; one JSON line."""
+    from nano_vllm_b200 import _native as nv
+
+    device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(device)
+    peaks = measured_peaks()
+    c = args.prior
+    cfg = chunk_config(c)
+    w = build_decode(cfg, 0, 1, device)
+    flops = 4 * 128 * 32 * 4 * sum(c + r + 1 for r in range(512))
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    times, out = time_launches(lambda: run_decode_step(w), args.steps, args.warmup, flush)
+    ms = statistics.median(times)
+    tf = flops / (ms * 1e-3) / 1e12
+    r = dict(metric="prefill attn TFLOPS", value=round(tf, 1), unit="TFLOP/s", ms=round(ms, 4),
+             workload=f"config2b chunked prefill 512 vs {c} paged", roofline_frac=round(tf / peaks["bf16"], 4),
+             spread=spread(times, flops, 1e12),
+             parity=parity_paged(w, out, np.array([0, 3]), one_head_per_group(32, 8)))
+    print(json.dumps(_single_line(r, args, peaks, "tensor", {"device_error_word": nv.device_error(device)})),
+          flush=True)
+
+
+def run_step(args):
+    """The 36-layer decode-step attention path alone (--steps timed steps); one JSON line."""
+    device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(device)
+    r = decode_step_results(device, B=args.batch or 64, steps=args.steps)
+    line = {"metric": r["metric"], "value": r["value"], "unit": r["unit"], "n_gpus": 1, "steps": args.steps,
+            "warmup": 3, "higher_is_better": False, "dtype": "bf16", "config": {"workload": r["workload"]},
+            "eager_us": r["eager_us"], "parity": r["parity"]}
+    print(json.dumps(line), flush=True)
+
+
 def run_ours(args):
     import torch.distributed as dist
 
     if args.config == "c2a":
         return run_prefill(args)
+    if args.config == "c2b":
+        return run_chunked(args)
+    if args.config == "step":
+        return run_step(args)
     if args.config == "qkprep":
         return run_qkprep(args)
     if args.config == "w4a16":
@@ -1288,7 +1326,9 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["c1", "c2a", "c3", "c4", "c5", "qkprep", "w4a16"], default="c3")
+    ap.add_argument("--config", choices=["c1", "c2a", "c2b", "c3", "c4", "c5", "qkprep", "w4a16", "step"],
+                    default="c3")
+    ap.add_argument("--prior", type=int, default=0, help="config 2b: paged tokens before the 512-token chunk")
     ap.add_argument("--batch", type=int, default=None, help="override the config's batch (small profiling cases)")
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")

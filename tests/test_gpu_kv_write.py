@@ -67,6 +67,48 @@ def test_int8_quantise_bit_exact(cuda, oracle, dtype):
             np.testing.assert_array_equal(sc[s // ps, :, s % ps], s_ref[t])
 
 
+def _tie_rows(dtype, gen):
+    """[8, 2, 128] rows whose x / s are exact half-integers: the amax element is
+    254/256 (so s = amax / 127 = 1/128 exactly) and the others are (2k + 1) / 256 with
+    random signs, i.e. x / s = k + 1/2.  In fp32, tokens 1 and 2 move every non-amax
+    element one ulp up / down (quotients just off the tie)."""
+    vals = torch.tensor([254.0 / 256] + [(2 * k + 1) / 256 for k in range(127)], dtype=torch.float64)
+    rows = []
+    for t in range(8):
+        sign = torch.where(torch.rand(2, 128, generator=gen) < 0.5, -1.0, 1.0).double()
+        x = vals.repeat(2, 1) * sign
+        if dtype == torch.float32 and t in (1, 2):
+            step = torch.full_like(x[:, 1:], float("inf") if t == 1 else 0.0).float()
+            x32 = x.float()
+            x32[:, 1:] = torch.nextafter(x32[:, 1:], torch.where(x32[:, 1:] > 0, step, -step))
+            x = x32.double()
+        rows.append(x)
+    return torch.stack(rows).to(dtype)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
+def test_int8_rounding_ties_bit_exact(cuda, oracle, dtype):
+    """Half-integer quotients (and one ulp either side of them): the division-free
+    rounding of the kernels must agree with round-half-even of the IEEE x / s."""
+    gen = torch.Generator().manual_seed(11)
+    x = _tie_rows(dtype, gen)
+    T, H, D, P, ps = 8, 2, 128, 2, 16
+    kp = torch.zeros(P, H, ps, D, dtype=torch.int8, device="cuda")
+    vp = torch.zeros_like(kp)
+    ks = torch.ones(P, H, ps, 1, dtype=dtype, device="cuda")
+    vs = torch.ones_like(ks)
+    slots = torch.arange(T, dtype=torch.int64) * 3
+    write_slots(x.cuda(), x.flip(0).cuda(), slots.cuda(), kp, vp, ks, vs)
+    code = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}[dtype]
+    for src, pages, scales in ((x, kp, ks), (x.flip(0), vp, vs)):
+        q_ref, s_ref = oracle.quantize_int8_ref(to_np(src), code)
+        pg, sc = to_np(pages), to_np(scales)
+        for t in range(T):
+            s = int(slots[t])
+            np.testing.assert_array_equal(pg[s // ps, :, s % ps], q_ref[t])
+            np.testing.assert_array_equal(sc[s // ps, :, s % ps], s_ref[t])
+
+
 def test_paged_cache_matches_full_cache(cuda):
     gen = torch.Generator().manual_seed(3)
     pool = TinyKvPagedPool(page_size=4)

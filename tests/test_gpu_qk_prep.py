@@ -272,3 +272,22 @@ def test_feeds_paged_decode(cuda, oracle, kv):
     else:
         ref = oracle.paged_attention_ref(q32, kpn, vpn, bt_np, cl_np, ps, kv_is_bf16=True)
     np.testing.assert_allclose(got.float().cpu().numpy(), ref, **TOL16)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=["bf16", "f16"])
+def test_int8_v_rounding_ties(cuda, oracle, dtype):
+    """V rows are quantised as given: rows whose x / s are exact half-integers must round
+    half to even exactly as the oracle's IEEE x / s does."""
+    B, L, Hq, Hkv, D, P, ps, eps = 1, 8, 16, 8, 128, 4, 16, 1e-6
+    rope = RoPE(D, 4096, 1000000, False, device=cuda)
+    pr = _problem(3, B, L, Hq, Hkv, D, dtype, torch.int8, P, ps, [7])
+    gen = torch.Generator().manual_seed(5)
+    vals = torch.tensor([254.0 / 256] + [(2 * k + 1) / 256 for k in range(127)], dtype=torch.float64)
+    sign = torch.where(torch.rand(B, L, Hkv, D, generator=gen) < 0.5, -1.0, 1.0).double()
+    pr["v"] = (vals * sign).to(dtype)
+    out, g = _run_gpu(pr, rope, eps, cuda)
+    _, err, kp, vp, ks, vs = _oracle(oracle, pr, rope, dtype, torch.int8, eps)
+    assert err == 0
+    np.testing.assert_array_equal(to_np(g["vp"]), vp)
+    np.testing.assert_array_equal(to_np(g["vs"]), vs)
+    np.testing.assert_array_equal(to_np(g["kp"]), kp)

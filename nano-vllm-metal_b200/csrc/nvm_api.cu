@@ -209,6 +209,7 @@ int nvm_paged_attention(const void* q, int q_dtype, const void* k_pages, const v
   if (B == 0) return NVM_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (!env_flag("NVM_ATTN_FORCE_GENERIC")) {
+    if (!env_flag("NVM_ATTN_NO_SM100") && flash2q_eligible(a)) return launch_flash2q(a, s);
     if (!env_flag("NVM_ATTN_NO_SM100")) {
       const Sm100Plan sp = plan_sm100(a, false);
       if (sp.eligible) {
@@ -251,6 +252,7 @@ int nvm_flash_attention(const void* q, const void* k, const void* v, int dtype, 
     a.B = B; a.Hq = Hq; a.Hkv = Hkv; a.L = L; a.D = D; a.P = B; a.page_size = S; a.max_pages = 1;
     a.scale = scale; a.is_causal = is_causal ? 1 : 0; a.dense = 1; a.dense_ctx = S;
     if (!env_flag("NVM_ATTN_NO_SM100")) {
+      if (flash2q_eligible(a)) return launch_flash2q(a, s);
       const Sm100Plan sp = plan_sm100(a, false);
       if (sp.eligible && sp.ws_bytes == 0) return launch_sm100(a, sp, nullptr, s);
     }

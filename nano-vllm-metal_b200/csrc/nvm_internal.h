@@ -101,6 +101,11 @@ struct Sm100Plan {
 Sm100Plan plan_sm100(const PagedArgs& a, bool sizing_only);
 int launch_sm100(const PagedArgs& a, const Sm100Plan& plan, void* ws, cudaStream_t s);
 
+// tcgen05 kernel with two 128-row query tiles per CTA (flash_2q.cu): prefill with at least
+// 256 query rows per head, 16-bit, D == 128; no workspace.
+bool flash2q_eligible(const PagedArgs& a);
+int launch_flash2q(const PagedArgs& a, cudaStream_t s);
+
 int launch_kv_write(const void* k, const void* v, int in_dtype, int64_t stride_t, int64_t stride_h,
                     void* k_pages, void* v_pages, int kv_dtype, void* k_scales, void* v_scales,
                     int scale_dtype, const int64_t* slot_mapping, int64_t T, int64_t Hkv, int64_t D,

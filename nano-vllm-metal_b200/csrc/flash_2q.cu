@@ -25,6 +25,12 @@
 // every earlier MMA of the thread, PV_t(j-1) included, has completed.
 // Every mbarrier wait is bounded; on expiry the CTA records an error, lets its own copies
 // and MMAs land (bounded), frees tensor memory and returns.
+//
+// Status: correct (tests/test_gpu_flash2q.py) but slower than flash_sm100.cu's one-tile
+// kernel on every shape measured, so it is taken only with NVM_ATTN_2Q=1.  With ten warps
+// the register cap is 168 per thread, which forces the softmax to read S in two 64-column
+// passes; moving half the exponentials to the FMA pipe made it slower still, so the
+// exponential unit is not what bounds it.
 #include <cstdlib>
 #include <mutex>
 
@@ -433,42 +439,49 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      float sv[kBN];
-#pragma unroll
-      for (int c = 0; c < kBN / 32; ++c) tmem_ld32(tS + c * 32, *reinterpret_cast<float(*)[32]>(&sv[c * 32]));
       const int pid_now = pid0;
       pid0 = pid1;
       pid1 = load_pid(j + 2);
-      tmem_wait_ld();
       const int64_t key0 = (int64_t)j * kBN;
       // only tiles that cross some row's last visible key pay for the mask
       const int64_t vis64 = last_key - key0;
-      if (__any_sync(0xffffffffu, vis64 < kBN - 1)) {
-        const int vis = vis64 < -1 ? -1 : (int)vis64;
+      const bool need_mask = __any_sync(0xffffffffu, vis64 < kBN - 1);
+      const int vis = vis64 < -1 ? -1 : (vis64 > kBN ? kBN : (int)vis64);
+      uint32_t holes = 0;
+      if (!p.dense)  // the 16-token groups of missing pages are masked
+        holes = __ballot_sync(0xffffffffu, lane < kPagesPerTile && (pid_now < 0 || pid_now >= (int)p.P)) & 0xFFu;
+      // 64 scores of the row (columns c0 .. c0 + 63) from TMEM, masked
+      auto load64 = [&](float (&sv)[64], int c0) {
+        tmem_ld32(tS + c0, *reinterpret_cast<float(*)[32]>(&sv[0]));
+        tmem_ld32(tS + c0 + 32, *reinterpret_cast<float(*)[32]>(&sv[32]));
+        tmem_wait_ld();
+        if (need_mask) {
 #pragma unroll
-        for (int c = 0; c < kBN; ++c) sv[c] = c <= vis ? sv[c] : -INFINITY;
-      }
-      if (!p.dense) {  // holes: the 16-token groups of missing pages are masked
-        const uint32_t holes =
-            __ballot_sync(0xffffffffu, lane < kPagesPerTile && (pid_now < 0 || pid_now >= (int)p.P)) & 0xFFu;
+          for (int c = 0; c < 64; ++c) sv[c] = c0 + c <= vis ? sv[c] : -INFINITY;
+        }
         if (holes != 0) {
 #pragma unroll
-          for (int gg = 0; gg < kPagesPerTile; ++gg) {
-            if ((holes >> gg) & 1u) {
+          for (int gg = 0; gg < 4; ++gg) {
+            if ((holes >> (c0 / 16 + gg)) & 1u) {
 #pragma unroll
               for (int c = 0; c < 16; ++c) sv[gg * 16 + c] = -INFINITY;
             }
           }
         }
-      }
-      // row max as a tree (8 independent chains)
+      };
+      // pass 1: the row max, 64 scores at a time (8 independent chains)
       float mv[8];
 #pragma unroll
-      for (int x = 0; x < 8; ++x) mv[x] = sv[x];
+      for (int x = 0; x < 8; ++x) mv[x] = -INFINITY;
+#pragma unroll 1
+      for (int c0 = 0; c0 < kBN; c0 += 64) {
+        float sv[64];
+        load64(sv, c0);
 #pragma unroll
-      for (int c = 8; c < kBN; c += 8) {
+        for (int c = 0; c < 64; c += 8) {
 #pragma unroll
-        for (int x = 0; x < 8; ++x) mv[x] = fmaxf(mv[x], sv[c + x]);
+          for (int x = 0; x < 8; ++x) mv[x] = fmaxf(mv[x], sv[c + x]);
+        }
       }
       const float mx = fmaxf(fmaxf(fmaxf(mv[0], mv[1]), fmaxf(mv[2], mv[3])),
                              fmaxf(fmaxf(mv[4], mv[5]), fmaxf(mv[6], mv[7])));
@@ -486,40 +499,42 @@ __global__ void __launch_bounds__(kThreads, 1)
       float2 acc[4];
 #pragma unroll
       for (int x = 0; x < 4; ++x) acc[x] = make_float2(0.f, 0.f);
+      // pass 2: p = 2^(s * sl2 - mu), the row sum, and P over the first columns of S_t:
+      // packed pairs, hi in [0, kBN/2); for split tiles the rounding residual p - hi as
+      // lo in [kBN/2, kBN).  The lo of the first half lands in columns the second half's
+      // scores still occupy, so it is stored after they have been read.
+      uint32_t lo_prev[32];
 #pragma unroll
-      for (int q = 0; q < kBN / 2; ++q) {
-        const float2 x2 = __ffma2_rn(make_float2(sv[2 * q], sv[2 * q + 1]), sl2v, nmu);
-        const float2 e = make_float2(ex2_ftz(x2.x), ex2_ftz(x2.y));
-        sv[2 * q] = e.x;
-        sv[2 * q + 1] = e.y;
-        acc[q & 3] = __fadd2_rn(acc[q & 3], e);
+      for (int h = 0; h < 2; ++h) {
+        float sv[64];
+        load64(sv, 64 * h);
+        if (split && h == 1) tmem_st32u(tS + kBN / 2, lo_prev);
+#pragma unroll
+        for (int q = 0; q < 32; ++q) {
+          const float2 x2 = __ffma2_rn(make_float2(sv[2 * q], sv[2 * q + 1]), sl2v, nmu);
+          const float2 e = make_float2(ex2_ftz(x2.x), ex2_ftz(x2.y));
+          sv[2 * q] = e.x;
+          sv[2 * q + 1] = e.y;
+          acc[q & 3] = __fadd2_rn(acc[q & 3], e);
+        }
+        uint32_t pk[32];
+#pragma unroll
+        for (int x = 0; x < 32; ++x) pk[x] = cvt_pack<T>(sv[2 * x], sv[2 * x + 1]);
+        tmem_st32u(tS + h * 32, pk);
+        if (split) {
+#pragma unroll
+          for (int x = 0; x < 32; ++x) {
+            // bf16 -> f32 is exact: the bf16 bits become the high half of the f32
+            const float h0 = __uint_as_float(pk[x] << 16), h1 = __uint_as_float(pk[x] & 0xFFFF0000u);
+            lo_prev[x] = cvt_pack<T>(sv[2 * x] - h0, sv[2 * x + 1] - h1);
+          }
+          if (h == 1) tmem_st32u(tS + kBN / 2 + 32, lo_prev);
+        }
       }
       const float2 a01 = __fadd2_rn(__fadd2_rn(acc[0], acc[1]), __fadd2_rn(acc[2], acc[3]));
       const float rs = m_ref == -INFINITY ? 0.f : a01.x + a01.y;
       lsum = (m == -INFINITY ? 0.f : lsum * alpha) + rs;
       m = m_ref;
-      // P over the first columns of S_t: packed pairs, hi in [0, kBN/2); for split tiles the
-      // rounding residual p - hi (computed in place) as lo in [kBN/2, kBN)
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        uint32_t pk[32];
-#pragma unroll
-        for (int x = 0; x < 32; ++x) pk[x] = cvt_pack<T>(sv[64 * h + 2 * x], sv[64 * h + 2 * x + 1]);
-        if (split) {
-#pragma unroll
-          for (int x = 0; x < 32; ++x) {
-            // bf16 -> f32 is exact: the bf16 bits become the high half of the f32
-            sv[64 * h + 2 * x] -= __uint_as_float(pk[x] << 16);
-            sv[64 * h + 2 * x + 1] -= __uint_as_float(pk[x] & 0xFFFF0000u);
-          }
-        }
-        tmem_st32u(tS + h * 32, pk);
-        if (split) {
-#pragma unroll
-          for (int x = 0; x < 32; ++x) pk[x] = cvt_pack<T>(sv[64 * h + 2 * x], sv[64 * h + 2 * x + 1]);
-          tmem_st32u(tS + kBN / 2 + h * 32, pk);
-        }
-      }
       if (__any_sync(0xffffffffu, rescale)) {
         // S_t(j) landed, so every earlier MMA of the issuing thread (PV_t(j-1) included)
         // has completed; PV_t(j) waits for this warpgroup's P_t(j) arrival below, so O_t
@@ -598,7 +613,9 @@ int launch_typed(dim3 grid, const CUtensorMap& tq, const CUtensorMap& tk, const 
 }  // namespace
 
 bool flash2q_eligible(const PagedArgs& a) {
-  if (env_i64("NVM_ATTN_NO_2Q", 0) != 0) return false;
+  // Opt-in (NVM_ATTN_2Q=1): measured slower than the one-tile kernel of flash_sm100.cu on
+  // every prefill shape tried (config 2a causal 594 vs 707 TFLOP/s bf16, 696 vs 754 fp16).
+  if (env_i64("NVM_ATTN_2Q", 0) == 0) return false;
   if (a.kv_dtype != NVM_F16 && a.kv_dtype != NVM_BF16) return false;
   if (a.q_dtype != a.kv_dtype || a.D != kD || !(a.scale > 0.f)) return false;
   if (a.L < 2 * kBM) return false;  // at least two query tiles per head

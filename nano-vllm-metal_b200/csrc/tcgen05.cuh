@@ -144,4 +144,34 @@ __device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t (&r)[3
 }
 
 
+// 2^x for two floats on the FMA pipe: n = round(x) through the 1.5 * 2^23 rounding
+// constant, f = x - n in [-0.5, 0.5] (exact), 2^f from a polynomial, then n is added to
+// the exponent field.  The coefficients are a near-minimax fit of 2^f on [-0.5, 0.5]
+// for relative error (iteratively reweighted least squares): degree 3 (7.5e-5, far below
+// the bf16 rounding of P that follows) for bf16, degree 4 (2.7e-6) for fp16.  Inputs
+// below -125 (masked scores, -inf) give 2^-125.
+template <typename T>
+__device__ __forceinline__ float2 exp2_fma2(float2 x) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  x.x = fmaxf(x.x, -125.f);
+  x.y = fmaxf(x.y, -125.f);
+  const float2 t = __fadd2_rn(x, make_float2(kRound, kRound));
+  const float2 n = __fadd2_rn(t, make_float2(-kRound, -kRound));
+  const float2 f = __ffma2_rn(n, make_float2(-1.f, -1.f), x);
+  float2 p;
+  if (std::is_same<T, __half>::value) {
+    p = __ffma2_rn(make_float2(0.009570102f, 0.009570102f), f, make_float2(0.05591786f, 0.05591786f));
+    p = __ffma2_rn(p, f, make_float2(0.24024744f, 0.24024744f));
+    p = __ffma2_rn(p, f, make_float2(0.69312179f, 0.69312179f));
+    p = __ffma2_rn(p, f, make_float2(0.99999928f, 0.99999928f));
+  } else {
+    p = __ffma2_rn(make_float2(0.05517167f, 0.05517167f), f, make_float2(0.24261113f, 0.24261113f));
+    p = __ffma2_rn(p, f, make_float2(0.69326097f, 0.69326097f));
+    p = __ffma2_rn(p, f, make_float2(0.99992806f, 0.99992806f));
+  }
+  // t's low mantissa bits hold n (two's complement); << 23 moves them to the exponent
+  return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(t.x) << 23)),
+                     __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23)));
+}
+
 }  // namespace nvm

@@ -1,7 +1,7 @@
 """GPU parity of the two-query-tile tcgen05 kernel (flash_2q.cu) against the oracle.
 
-Prefill with at least 256 query rows per head (16-bit, head dim 128) takes this
-kernel: one CTA per (q head, 256-row block), 128-key K/V tiles shared by both query
+With NVM_ATTN_2Q=1, prefill with at least 256 query rows per head (16-bit, head dim
+128) takes this kernel: one CTA per (q head, 256-row block), 128-key K/V tiles shared by both query
 tiles.  Dense causal / full attention (square and L < S, a partial last row block) and
 chunked prefill over paged context (holes, an empty sequence); the order check runs the
 MMA sequence with an explicit completion wait before each S overwrites P and must give
@@ -16,6 +16,12 @@ from nano_vllm_b200 import flash_attention, paged_attention
 from nano_vllm_b200 import _native as nv
 
 pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(autouse=True)
+def _two_tile_kernel(monkeypatch):
+    """The two-tile kernel is opt-in; every test here runs it."""
+    monkeypatch.setenv("NVM_ATTN_2Q", "1")
 
 DENSE = [(1, 4, 2, 256, 256), (2, 8, 2, 320, 320), (1, 4, 1, 300, 700), (1, 2, 1, 1024, 1024),
          (2, 4, 4, 512, 2048)]
@@ -81,6 +87,6 @@ def test_matches_one_tile_kernel(cuda, monkeypatch):
     prob = random_paged_problem(gen, 2, 16, 4, 384, 128, 16, torch.bfloat16, 600, 2000)
     args = (prob["q"], prob["kp"], prob["vp"], prob["bt"], prob["cl"], 16)
     a = paged_attention(*args, mask="causal")
-    monkeypatch.setenv("NVM_ATTN_NO_2Q", "1")
+    monkeypatch.setenv("NVM_ATTN_2Q", "0")
     b = paged_attention(*args, mask="causal")
     torch.testing.assert_close(a, b, atol=2e-3, rtol=1e-2)

@@ -217,6 +217,23 @@ __global__ void __launch_bounds__(Cfg<KvT, D, NWM, NWK, NS_>::kThreads)
     else
       load_q(__nv_bfloat16{});
   }
+  // n8 tile, int8 pages: K enters the mma as int8 + 1152 (the byte-permute alone, exact in
+  // f16), so every score carries 1152 * sum_d q[row][d] too; this lane's two rows'
+  // corrections (rows 2cq, 2cq+1), from the f16 q values the mma multiplies.
+  float kbias0 = 0.f, kbias1 = 0.f;
+  if constexpr (C::kN8 && C::kI8) {
+    float qs = 0.f;  // this lane's share of row r: d = 32 cq + 4 ks + {0..3}
+#pragma unroll
+    for (int ks = 0; ks < NKS; ++ks) {
+      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&qa[ks][0]));
+      const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&qa[ks][2]));
+      qs += (a.x + a.y) + (b.x + b.y);
+    }
+    qs += __shfl_xor_sync(0xffffffffu, qs, 1);
+    qs += __shfl_xor_sync(0xffffffffu, qs, 2);  // row r's sum on all four lanes of row r
+    kbias0 = 1152.f * __shfl_sync(0xffffffffu, qs, 4 * (2 * cq));
+    kbias1 = 1152.f * __shfl_sync(0xffffffffu, qs, 4 * (2 * cq + 1));
+  }
   if (warp == (C::kSelfFeed ? 0 : C::kCons)) {
     // The chunk's block-table entries, read together with (not after) the context
     // length: the row holds mp entries, so entries past the context are in bounds and
@@ -397,29 +414,30 @@ __global__ void __launch_bounds__(Cfg<KvT, D, NWM, NWK, NS_>::kThreads)
 #pragma unroll
         for (int ks = 0; ks < NKS; ++ks) {
           const uint32_t x0 = kw[0][ks] ^ 0x80808080u, x1 = kw[1][ks] ^ 0x80808080u;
-          const uint32_t a[4] = {i8pair_to_f16x2(x0, 0x4140u), i8pair_to_f16x2(x1, 0x4140u),
-                                 i8pair_to_f16x2(x0, 0x4342u), i8pair_to_f16x2(x1, 0x4342u)};
+          // f16 value 1024 + (byte ^ 0x80) = int8 + 1152 (the bias is removed below)
+          const uint32_t a[4] = {prmt(x0, 0x64646464u, 0x4140u), prmt(x1, 0x64646464u, 0x4140u),
+                                 prmt(x0, 0x64646464u, 0x4342u), prmt(x1, 0x64646464u, 0x4342u)};
           mma16816<MmaT>(sacc[ks & 1], a, qa[ks][0], qa[ks][2]);
         }
-        const ScaleT* ksp = reinterpret_cast<const ScaleT*>(smem + s * C::kStageBytes + 2 * C::kTileBytes);
-        const float k0 = to_f32(ksp[r]), k1 = to_f32(ksp[r + 8]);
-        sacc[0][0] *= k0;
-        sacc[0][1] *= k0;
-        sacc[0][2] *= k1;
-        sacc[0][3] *= k1;
-        sacc[1][0] *= k0;
-        sacc[1][1] *= k0;
-        sacc[1][2] *= k1;
-        sacc[1][3] *= k1;
       }
       // sv[0] = (key r, row 2cq), [1] = (key r, row 2cq+1), [2] = (key r+8, row 2cq), [3] = (key r+8, row 2cq+1)
       float sv[4];
+      if constexpr (C::kI8) {
+        // the +1152 bias of K removed per row, then each key's scale
+        const ScaleT* ksp = reinterpret_cast<const ScaleT*>(smem + s * C::kStageBytes + 2 * C::kTileBytes);
+        const float k0 = to_f32(ksp[r]), k1 = to_f32(ksp[r + 8]);
+        sv[0] = ((sacc[0][0] + sacc[1][0]) - kbias0) * k0;
+        sv[1] = ((sacc[0][1] + sacc[1][1]) - kbias1) * k0;
+        sv[2] = ((sacc[0][2] + sacc[1][2]) - kbias0) * k1;
+        sv[3] = ((sacc[0][3] + sacc[1][3]) - kbias1) * k1;
+      } else {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        if constexpr (kQc == 4)
-          sv[e] = (sacc[0][e] + sacc[1][e]) + (sacc[2][e] + sacc[3][e]);
-        else
-          sv[e] = sacc[0][e] + sacc[1][e];
+        for (int e = 0; e < 4; ++e) {
+          if constexpr (kQc == 4)
+            sv[e] = (sacc[0][e] + sacc[1][e]) + (sacc[2][e] + sacc[3][e]);
+          else
+            sv[e] = sacc[0][e] + sacc[1][e];
+        }
       }
       const bool need_mask = tok0 + 16 > clean;
 #pragma unroll
@@ -461,7 +479,16 @@ __global__ void __launch_bounds__(Cfg<KvT, D, NWM, NWK, NS_>::kThreads)
         }
       }
       // P^T as the B operand (keys x rows): each 8 x 8 quadrant of P^T's accumulator
-      // layout transposed in registers
+      // layout transposed in registers.  int8 pages: each key's value scale multiplies its
+      // P entries here (keys r and r + 8 of this lane), so V enters the mma unscaled.
+      if constexpr (C::kI8) {
+        const ScaleT* vsp = reinterpret_cast<const ScaleT*>(smem + s * C::kStageBytes + 2 * C::kTileBytes + 128);
+        const float v0 = to_f32(vsp[r]), v1 = to_f32(vsp[r + 8]);
+        sv[0] *= v0;
+        sv[1] *= v0;
+        sv[2] *= v1;
+        sv[3] *= v1;
+      }
       uint32_t pb[2], pbl[2];
       pb[0] = movmatrix_t(pack2<MmaT>(sv[0], sv[1]));
       pb[1] = movmatrix_t(pack2<MmaT>(sv[2], sv[3]));
@@ -491,9 +518,7 @@ __global__ void __launch_bounds__(Cfg<KvT, D, NWM, NWK, NS_>::kThreads)
           const int tok = 2 * cq + (t4 & 1) + (t4 >> 1) * 8;
           lds128(swz(vt, tok, r), vw[t4][0], vw[t4][1], vw[t4][2], vw[t4][3]);
         }
-        const ScaleT* vsp = reinterpret_cast<const ScaleT*>(smem + s * C::kStageBytes + 2 * C::kTileBytes + 128);
-        const __half2 vlo = __floats2half2_rn(to_f32(vsp[2 * cq]), to_f32(vsp[2 * cq + 1]));
-        const __half2 vhi = __floats2half2_rn(to_f32(vsp[2 * cq + 8]), to_f32(vsp[2 * cq + 9]));
+        // V enters unscaled (exact int8 -> f16); the value scales were folded into P^T
 #pragma unroll
         for (int w = 0; w < 4; ++w) {
           const uint32_t y01 = prmt(vw[0][w], vw[1][w], 0x5140u) ^ 0x80808080u;
@@ -503,14 +528,8 @@ __global__ void __launch_bounds__(Cfg<KvT, D, NWM, NWK, NS_>::kThreads)
 #pragma unroll
           for (int jj = 0; jj < 2; ++jj) {
             const uint32_t y = jj ? y23 : y01, z = jj ? z23 : z01;
-            uint32_t e0 = i8pair_to_f16x2(y, 0x4140u), e1 = i8pair_to_f16x2(y, 0x4342u);
-            uint32_t e2 = i8pair_to_f16x2(z, 0x4140u), e3 = i8pair_to_f16x2(z, 0x4342u);
-            __half2 f0 = __hmul2(*reinterpret_cast<__half2*>(&e0), vlo);
-            __half2 f1 = __hmul2(*reinterpret_cast<__half2*>(&e1), vlo);
-            __half2 f2 = __hmul2(*reinterpret_cast<__half2*>(&e2), vhi);
-            __half2 f3 = __hmul2(*reinterpret_cast<__half2*>(&e3), vhi);
-            const uint32_t a[4] = {*reinterpret_cast<uint32_t*>(&f0), *reinterpret_cast<uint32_t*>(&f1),
-                                   *reinterpret_cast<uint32_t*>(&f2), *reinterpret_cast<uint32_t*>(&f3)};
+            const uint32_t a[4] = {i8pair_to_f16x2(y, 0x4140u), i8pair_to_f16x2(y, 0x4342u),
+                                   i8pair_to_f16x2(z, 0x4140u), i8pair_to_f16x2(z, 0x4342u)};
             mma16816<MmaT>(o[2 * w + jj], a, pb[0], pb[1]);
           }
         }

@@ -30,6 +30,7 @@
 
 #include <cstdio>
 #include <cstdlib>
+#include <atomic>
 #include <mutex>
 
 #include "nvm_common.cuh"
@@ -46,6 +47,8 @@ constexpr int64_t kMaxUnits = (int64_t)(kCounterBytes / sizeof(int));
 constexpr int kDefaultDecodeVariant = 3;
 constexpr int kDefaultN8Variant = 7;  // c4 int8 prefers 4 (2 warps, 8 stages) by 1%
 constexpr int kDefaultM3Variant = 1;
+// longest chunk (16-key tiles) the one-wave sizing of the n8 tile hands a CTA
+constexpr int64_t kOneWaveTiles = 128;
 
 struct MmaParams {
   const void* q;
@@ -980,22 +983,93 @@ int64_t env_int(const char* name, int64_t dflt) {
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
+// Opts one kernel instance into its dynamic shared memory, once per device.
+template <typename KvT, typename ScaleT, int D, int NWM, int NWK, int NS_>
+int ensure_smem_attr() {
+  using C = Cfg<KvT, D, NWM, NWK, NS_>;
+  static std::mutex mu;
+  static uint64_t done_mask = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (dev < 64 && !(done_mask & (1ull << dev))) {
+    int st = check_cuda(cudaFuncSetAttribute(paged_mma_kernel<KvT, ScaleT, D, NWM, NWK, NS_>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes),
+                        "paged_attention: cudaFuncSetAttribute");
+    if (st != NVM_OK) return st;
+    done_mask |= 1ull << dev;
+  }
+  return NVM_OK;
+}
+
+// CTAs of one n8 kernel instance resident on an SM (registers and shared memory), asked
+// of the runtime once; without a device (workspace sizing on a host) the shared-memory
+// bound, at most 8 (the register bound of the instances built here: <= 128 a thread).
+template <typename KvT, typename ScaleT, int D, int NWK, int NS_>
+int n8_resident() {
+  using C = Cfg<KvT, D, 0, NWK, NS_>;
+  static std::atomic<int> cached{0};
+  int n = cached.load(std::memory_order_relaxed);
+  if (n > 0) return n;
+  n = 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || ensure_smem_attr<KvT, ScaleT, D, 0, NWK, NS_>() != NVM_OK ||
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, paged_mma_kernel<KvT, ScaleT, D, 0, NWK, NS_>, C::kThreads,
+                                                    C::kSmemBytes) != cudaSuccess ||
+      n <= 0) {
+    cudaGetLastError();
+    n = 233472 / (C::kSmemBytes + 1024);
+    n = n < 1 ? 1 : (n > 8 ? 8 : n);
+    return n;  // not cached: a later call with a device asks the runtime
+  }
+  cached.store(n, std::memory_order_relaxed);
+  return n;
+}
+
+template <typename KvT, typename ScaleT, int D>
+int n8_resident_variant(int variant) {
+  switch (variant) {  // the (NWK, NS) of each variant, as launch_decode maps them
+    case 0: return n8_resident<KvT, ScaleT, D, 4, 0>();
+    case 1: return n8_resident<KvT, ScaleT, D, 4, 12>();
+    case 2: return n8_resident<KvT, ScaleT, D, 2, 2>();
+    case 4: return n8_resident<KvT, ScaleT, D, 2, 8>();
+    case 6: return n8_resident<KvT, ScaleT, D, 1, 4>();
+    case 7: return n8_resident<KvT, ScaleT, D, 2, 4>();
+    case 8: return n8_resident<KvT, ScaleT, D, 1, 6>();
+    default: return n8_resident<KvT, ScaleT, D, 2, 6>();
+  }
+}
+
+int n8_resident_per_sm(const PagedArgs& a, int variant) {
+  if (a.kv_dtype == NVM_I8) return n8_resident_variant<int8_t, __half, 128>(variant);
+  if (a.kv_dtype == NVM_F16)
+    return a.D == 64 ? n8_resident_variant<__half, __half, 64>(variant) : n8_resident_variant<__half, __half, 128>(variant);
+  return a.D == 64 ? n8_resident_variant<__nv_bfloat16, __nv_bfloat16, 64>(variant)
+                   : n8_resident_variant<__nv_bfloat16, __nv_bfloat16, 128>(variant);
+}
+
+int sm_count_cached() {
+  static std::atomic<int> cached{0};
+  int n = cached.load(std::memory_order_relaxed);
+  if (n > 0) return n;
+  int dev = 0;
+  n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+      n <= 0) {
+    cudaGetLastError();
+    return 148;
+  }
+  cached.store(n, std::memory_order_relaxed);
+  return n;
+}
+
 template <typename KvT, typename ScaleT, int D, int NWM, int NWK, int NS_ = 0>
 int launch_cfg(const PagedArgs& a, const MmaPlan& plan, void* ws, cudaStream_t s) {
   using C = Cfg<KvT, D, NWM, NWK, NS_>;
   auto kern = paged_mma_kernel<KvT, ScaleT, D, NWM, NWK, NS_>;
   {
-    static std::mutex mu;
-    static uint64_t done_mask = 0;
-    int dev = 0;
-    cudaGetDevice(&dev);
-    std::lock_guard<std::mutex> lock(mu);
-    if (dev < 64 && !(done_mask & (1ull << dev))) {
-      int st = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes),
-                          "paged_attention: cudaFuncSetAttribute");
-      if (st != NVM_OK) return st;
-      done_mask |= 1ull << dev;
-    }
+    const int st = ensure_smem_attr<KvT, ScaleT, D, NWM, NWK, NS_>();
+    if (st != NVM_OK) return st;
   }
   // Tensor maps: pools [P, Hkv, ps, D] -> dims (D, ps, Hkv, P); scales [P, Hkv, ps] -> (ps, Hkv, P).
   const CUtensorMapDataType dt = C::kI8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
@@ -1168,11 +1242,42 @@ MmaPlan plan_paged_mma(const PagedArgs& a) {
     // fewer waves the last one runs mostly idle (config 4, 64 sequences of 8K-32K keys:
     // 160-tile chunks 4777-4807 GB/s against 4533-4564 with 256; config 3 stays at the
     // 256 cap).  Multi-row tiles keep about 16 chunk CTAs per SM.
-    const int64_t target = plan.nwm == 0 ? 148 * 48 : 148 * 16;
+    const int64_t sms = sm_count_cached();
+    const int64_t target = plan.nwm == 0 ? sms * 48 : sms * 16;
     ct = (plan.n_units * tiles_max + target - 1) / target;
     ct = ((ct + 15) / 16) * 16;
     if (ct < 16) ct = 16;
     if (ct > kMaxChunkTiles) ct = kMaxChunkTiles;
+    // Short contexts (the n8 tile): many 16-tile chunks cost more in per-CTA set-up,
+    // merges and partial waves than they gain in balance.  When the units fit in the
+    // CTA slots the SMs hold at once, each is cut into the fewest equal chunks that give
+    // about four CTAs per SM (enough page loads in flight to keep HBM busy), within one
+    // wave, if those chunks are at most kOneWaveTiles long: B = 64 at 1-1.1K keys (32/8
+    // heads) one 70-tile chunk a unit, 50.5 us against 65.5 us with five 14-tile chunks;
+    // B = 32 at 2K keys three 44-tile chunks, 53 us against 66 us.  Otherwise chunks are
+    // at least 48 tiles long (B = 128 at 1-1.1K keys: 2 x 35 tiles, 105 us against
+    // 121 us; B = 256 at 512 keys: one 36-tile chunk, 104 us against 132 us).
+    // NVM_ATTN_WAVE_RULE=0 keeps the six-wave sizing alone (sweeps).
+    if (plan.nwm == 0 && env_int("NVM_ATTN_WAVE_RULE", 1) != 0) {
+      const int64_t slots = sms * n8_resident_per_sm(a, plan.variant);
+      bool one_wave = false;
+      if (plan.n_units <= slots) {
+        int64_t nc = (4 * sms + plan.n_units - 1) / plan.n_units;
+        const int64_t nc_max = slots / plan.n_units;
+        if (nc > nc_max) nc = nc_max;
+        if (nc < 1) nc = 1;
+        int64_t ct1 = (tiles_max + nc - 1) / nc;
+        if (ct1 < 16) ct1 = 16;
+        if (ct1 <= kOneWaveTiles) {
+          ct = ct1;
+          one_wave = true;
+        }
+      }
+      if (!one_wave) {
+        const int64_t floor_ct = tiles_max < 48 ? tiles_max : 48;
+        if (ct < floor_ct) ct = floor_ct;
+      }
+    }
     // the longest context split evenly over that many chunks (B = 512 at 1024 tokens:
     // 2 x 32 tiles, 343 us, instead of 48 + 16, 391 us)
     if (ct < tiles_max) {
@@ -1193,16 +1298,17 @@ MmaPlan plan_paged_mma(const PagedArgs& a) {
   // (distributed shared memory) instead of through the workspace, which takes the
   // global-memory round trips of the split-K merge off every unit's critical path.
   // Every CTA of a cluster stays resident until its unit is merged, so chunks without
-  // keys (ragged contexts) idle in their slots; the cluster merge is therefore used
-  // when the launch fits in one wave (about six n8 CTAs per SM) or a unit has at most
-  // four chunks.
+  // keys (ragged contexts) idle in their slots, and a cluster launches only when all
+  // its CTAs fit at once; the cluster merge is therefore used when the launch fits in
+  // one wave (B = 128 at 1-1.1K keys, 2 chunks over two waves: 125 us in clusters
+  // against 105 us through the workspace).
   // NVM_ATTN_CLUSTER: 0 never, 2 whenever 2..8 chunks (sweeps), otherwise the rule above.
   plan.cluster = 0;
   const int64_t cl_mode = env_int("NVM_ATTN_CLUSTER", 1);
   if (plan.nwm == 0 && plan.nwk <= 4 && !dense && can_split && plan.n_chunks >= 2 && plan.n_chunks <= 8 &&
       cl_mode != 0) {
-    const bool one_wave = plan.n_units * plan.n_chunks <= 148 * 6;
-    if (cl_mode == 2 || one_wave || plan.n_chunks <= 4) plan.cluster = 1;
+    const bool one_wave = plan.n_units * plan.n_chunks <= sm_count_cached() * n8_resident_per_sm(a, plan.variant);
+    if (cl_mode == 2 || one_wave) plan.cluster = 1;
   }
   if (dense && ct > kMaxChunkTiles) {
     // The per-CTA page table holds kMaxChunkTiles entries; a dense sequence longer

@@ -40,9 +40,10 @@ def _args(prob, out):
 
 
 # (B, Hq, Hkv, L, context range): an L = 1 decode (g * L = 4 rows per kv head, the
-# mma.sync kernel) and an L = 4 verify-like call (g * L = 16 rows: the tcgen05 grouped
-# mode, split over key chunks with its persistent work counters)
-CASES = {"decode_mma": (24, 32, 8, 1, 2000, 6000), "grouped_tcgen05": (16, 32, 8, 4, 6000, 12000)}
+# mma.sync kernel; 1280 units, more than the SMs hold at once, so each is split into two
+# chunks merged through the scratch) and an L = 4 verify-like call (g * L = 16 rows: the
+# tcgen05 grouped mode, split over key chunks with its persistent work counters)
+CASES = {"decode_mma": (160, 32, 8, 1, 600, 1000), "grouped_tcgen05": (16, 32, 8, 4, 6000, 12000)}
 
 
 @pytest.mark.parametrize("case", sorted(CASES))
@@ -89,17 +90,17 @@ _FRESH_PROCESS = textwrap.dedent("""
     torch.cuda.set_device(dev)
     gen = torch.Generator().manual_seed(5)
     short = random_paged_problem(gen, 2, 32, 8, 1, 128, 16, torch.bfloat16, 40, 60)
-    long_ = random_paged_problem(gen, 24, 32, 8, 1, 128, 16, torch.bfloat16, 2000, 6000)
+    long_ = random_paged_problem(gen, 160, 32, 8, 1, 128, 16, torch.bfloat16, 600, 1000)
     mp_s, mp_l = short["bt"].shape[1], long_["bt"].shape[1]
     out_s = torch.empty(2, 32, 1, 128, dtype=torch.float32, device=dev)
-    out_l = torch.empty(24, 32, 1, 128, dtype=torch.float32, device=dev)
+    out_l = torch.empty(160, 32, 1, 128, dtype=torch.float32, device=dev)
     ref = torch.empty_like(out_l)
     ws = torch.zeros(64 << 20, dtype=torch.uint8, device=dev)
     torch.cuda.synchronize()
     free0 = torch.cuda.mem_get_info(dev)[0]
     L = nv.lib()
     assert L.nvm_paged_attention_workspace_size(2, 32, 8, 1, 128, 16, mp_s, nv.NVM_BF16) == 0
-    need = L.nvm_paged_attention_workspace_size(24, 32, 8, 1, 128, 16, mp_l, nv.NVM_BF16)
+    need = L.nvm_paged_attention_workspace_size(160, 32, 8, 1, 128, 16, mp_l, nv.NVM_BF16)
     assert 0 < need <= ws.numel()
     stream = nv.stream_ptr(dev)
     # the first call on the device needs no scratch and sets up the array all the same

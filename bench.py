@@ -1048,8 +1048,8 @@ def _single_line(r: dict, args, peaks: dict, bound: str, extra: dict | None = No
 
 
 def run_qkprep(args):
-    """The fused q/k-norm + RoPE + K/V write alone (bf16 pools), 4 x 2048 tokens unless
-    --batch says otherwise; one JSON line."""
+    """The fused q/k-norm + RoPE + K/V write alone (bf16 or, with --kv int8, int8 pools),
+    4 x 2048 tokens unless --batch says otherwise; one JSON line."""
     from nano_vllm_b200 import _native as nv
 
     device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
@@ -1057,7 +1057,7 @@ def run_qkprep(args):
     peaks = measured_peaks()
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
     r = qk_prep_results(peaks, device, flush, B=args.batch or 4, iters=args.steps, warmup=args.warmup,
-                        kinds=("bf16",))[0]
+                        kinds=(args.kv,))[0]
     print(json.dumps(_single_line(r, args, peaks, "hbm", {"device_error_word": nv.device_error(device)})), flush=True)
 
 
@@ -1345,6 +1345,7 @@ def main():
                     default="c3")
     ap.add_argument("--prior", type=int, default=0, help="config 2b: paged tokens before the 512-token chunk")
     ap.add_argument("--batch", type=int, default=None, help="override the config's batch (small profiling cases)")
+    ap.add_argument("--kv", choices=["bf16", "int8"], default="bf16", help="qkprep: page pool dtype")
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=8.0)

@@ -44,11 +44,8 @@ __device__ __forceinline__ void quantize_row(const void* src, int64_t src_off, i
   for (int64_t d = lane; d < D; d += 32) amax = fmaxf(amax, fabsf(load_dyn(src, src_off + d, in_dtype)));
   amax = warp_max(amax);
   const float s = amax > 0.0f ? __fdiv_rn(amax, 127.0f) : 1.0f;
-  for (int64_t d = lane; d < D; d += 32) {
-    float y = rintf(__fdiv_rn(load_dyn(src, src_off + d, in_dtype), s));
-    y = fminf(fmaxf(y, -127.0f), 127.0f);
-    dst[d] = (int8_t)(int)y;
-  }
+  const float r = __frcp_rn(s);
+  for (int64_t d = lane; d < D; d += 32) dst[d] = (int8_t)quantize_i8(load_dyn(src, src_off + d, in_dtype), s, r);
   if (lane == 0) store_dyn(scales, scale_idx, scale_dtype, s);
 }
 

@@ -100,6 +100,37 @@ __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// int8 quantisation of x with row scale s = fl(amax / 127) (1 when amax == 0) and its
+// reciprocal r = fl(1 / s): clip(rint(fl(x / s)), -127, 127), round half to even, as the
+// reference's fp32 quotient.  |x| <= amax gives |x / s| <= 128, so t = fl(x * r) is within
+// 2^-16 of x / s (two roundings of relative size 2^-24) and within 2^-15 of fl(x / s)
+// (half an ulp below 128 is 2^-18).  If t lies at least 2^-14 from every half-integer, t
+// and fl(x / s) are on the same side of it and round to the same integer.
+//
+// quantize_i8_fast rounds t through the 1.5 * 2^23 shifter (t + 1.5 * 2^23 is rounded to
+// nearest even at unit spacing for |t| < 2^22) and reads the integer from the sum's low
+// bits, so no conversion unit is involved; `amb` marks values within 2^-14 of a
+// half-integer (and NaN), which the caller sends to quantize_i8_div.
+__device__ __forceinline__ int quantize_i8_fast(float x, float r, bool& amb) {
+  const float t = __fmul_rn(x, r);
+  const float f = __fadd_rn(t, 12582912.0f);
+  const float n = __fsub_rn(f, 12582912.0f);
+  amb = !(fabsf(__fsub_rn(t, n)) < 0.5f - 0x1p-14f);
+  const int q = __float_as_int(f) - 0x4B400000;
+  return min(max(q, -127), 127);
+}
+
+__device__ __forceinline__ int quantize_i8_div(float x, float s) {
+  const float y = rintf(__fdiv_rn(x, s));
+  return (int)fminf(fmaxf(y, -127.0f), 127.0f);
+}
+
+__device__ __forceinline__ int quantize_i8(float x, float s, float r) {
+  bool amb;
+  const int q = quantize_i8_fast(x, r, amb);
+  return amb ? quantize_i8_div(x, s) : q;
+}
+
 // ---------------------------------------------------------------------------
 // shared memory, mbarrier, timers
 // ---------------------------------------------------------------------------

@@ -138,21 +138,32 @@ __device__ __forceinline__ float reduce8(const float (&v)[8], int lane) {
   return d;
 }
 
-// int8 quantisation of one lane's 2*EH values of a row whose scale s is known (same
-// arithmetic as kv_write.cu: IEEE division, round half to even, clip to [-127, 127])
+// int8 quantisation of one lane's 2*EH values of a row (both halves) whose scale s and
+// its reciprocal r are known, written at dst + lo and dst + hi (same arithmetic as
+// kv_write.cu: the quotient x / s rounded half to even and clipped to [-127, 127]).  The
+// rare values near a half-integer are divided under one warp vote.
 template <int EH>
-__device__ __forceinline__ void quantize_half(const float* x, float s, int8_t* dst) {
-  uint32_t packed = 0;
+__device__ __forceinline__ void quantize_row_lane(const float* x, float s, float r, int8_t* dst, int lo, int hi) {
+  int q[2 * EH];
+  bool amb[2 * EH];
+  bool any = false;
 #pragma unroll
-  for (int e = 0; e < EH; ++e) {
-    float y = rintf(__fdiv_rn(x[e], s));
-    y = fminf(fmaxf(y, -127.0f), 127.0f);
-    packed |= (uint32_t)(uint8_t)(int8_t)(int)y << (8 * e);
+  for (int e = 0; e < 2 * EH; ++e) {
+    q[e] = quantize_i8_fast(x[e], r, amb[e]);
+    any |= amb[e];
   }
-  if constexpr (EH == 2)
-    *reinterpret_cast<uint16_t*>(dst) = (uint16_t)packed;
-  else
-    *dst = (int8_t)packed;
+  if (__any_sync(0xffffffffu, any)) {
+#pragma unroll
+    for (int e = 0; e < 2 * EH; ++e)
+      if (amb[e]) q[e] = quantize_i8_div(x[e], s);
+  }
+  if constexpr (EH == 2) {
+    *reinterpret_cast<uint16_t*>(dst + lo) = (uint16_t)((q[0] & 0xff) | ((q[1] & 0xff) << 8));
+    *reinterpret_cast<uint16_t*>(dst + hi) = (uint16_t)((q[2] & 0xff) | ((q[3] & 0xff) << 8));
+  } else {
+    dst[lo] = (int8_t)q[0];
+    dst[hi] = (int8_t)q[1];
+  }
 }
 
 // Lane layout: lane l holds elements [l*EH, (l+1)*EH) of the first half of a row and the
@@ -281,16 +292,16 @@ __device__ __forceinline__ void quantize_batch(const typename Lane<T, D>::V (&rl
   }
   const float amax_mine = reduce8<true>(red, lane);
   const float s_mine = amax_mine > 0.0f ? __fdiv_rn(amax_mine, 127.0f) : 1.0f;
+  const float r_mine = __frcp_rn(s_mine);
 #pragma unroll
   for (int i = 0; i < kBatch; ++i) {
     const float sc = __shfl_sync(0xffffffffu, s_mine, i * 4);
+    const float rc = __shfl_sync(0xffffffffu, r_mine, i * 4);
     if (h0 + i >= count) break;  // warp-uniform
     float x[2 * EH];
     unpack<T, EH>(rlo[i], x);
     unpack<T, EH>(rhi[i], x + EH);
-    int8_t* dst = pool_row0 + (int64_t)(h0 + i) * row_stride;
-    quantize_half<EH>(x, sc, dst + lo);
-    quantize_half<EH>(x + EH, sc, dst + hi);
+    quantize_row_lane<EH>(x, sc, rc, pool_row0 + (int64_t)(h0 + i) * row_stride, lo, hi);
     if (lane == 0) store_dyn(scales, srow0 + (int64_t)(h0 + i) * srow_stride, scale_dtype, sc);
   }
 }
@@ -477,11 +488,15 @@ int launch_t(const QkPrepParams& p, int64_t D, cudaStream_t s) {
       sms = n;
     if (sms <= 0) sms = 148;
   }
-  // segments per token: enough units for about four per resident warp
+  // segments per token: about one unit per resident warp.  With int8 pools the segment
+  // holding the k and v rows (quantised) outweighs the others, and whole tokens per warp
+  // won once there are a quarter as many tokens as warps (8192 tokens: 2636 GB/s against
+  // 2147 with two segments; 2048 tokens: 1924 against 1539).
   const int64_t nb = (p.Hq + kBatch - 1) / kBatch + 2 * ((p.Hkv + kBatch - 1) / kBatch);
   const int64_t warps_cap = (int64_t)sms * kBlocksPerSm * kWarps;
   QkPrepParams q = p;
-  q.segs = (int)std::min<int64_t>(nb, std::max<int64_t>(1, (4 * warps_cap + p.T - 1) / std::max<int64_t>(p.T, 1)));
+  q.segs = (int)std::min<int64_t>(nb, std::max<int64_t>(1, (warps_cap + p.T - 1) / std::max<int64_t>(p.T, 1)));
+  if (p.kv_dtype == NVM_I8 && 4 * p.T >= warps_cap) q.segs = 1;
   static const int64_t segs_env = env_int("NVM_QKPREP_SEGS", 0);
   if (segs_env > 0) q.segs = (int)std::min<int64_t>(nb, segs_env);
   const int64_t blocks_needed = (p.T * q.segs + kWarps - 1) / kWarps;

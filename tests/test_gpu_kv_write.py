@@ -109,6 +109,47 @@ def test_int8_rounding_ties_bit_exact(cuda, oracle, dtype):
             np.testing.assert_array_equal(sc[s // ps, :, s % ps], s_ref[t])
 
 
+def _near_tie_rows(gen, T, H, D):
+    """fp32 rows with random non-power-of-two scales whose quotients x / s sit within a
+    few ulps of half-integers: amax A in [0.5, 100) as element 0, the others
+    fl((k + 1/2) * fl(A / 127)) moved by -4..4 ulps, k in [-126, 125]."""
+    A = (torch.rand(T, H, 1, generator=gen, dtype=torch.float64) * 99.5 + 0.5).float()
+    s = (A.double() / 127).float().double()
+    k = torch.randint(-126, 126, (T, H, D), generator=gen).double()
+    x = ((k + 0.5) * s).float()
+    n = torch.randint(-4, 5, (T, H, D), generator=gen)
+    for step in range(4):
+        up = n > step
+        down = n < -step
+        x = torch.where(up, torch.nextafter(x, torch.full_like(x, float("inf"))), x)
+        x = torch.where(down, torch.nextafter(x, torch.full_like(x, -float("inf"))), x)
+    x[:, :, 0] = A[:, :, 0] * torch.where(torch.rand(T, H, generator=gen) < 0.5, -1.0, 1.0)
+    return x
+
+
+def test_int8_near_ties_random_scales_bit_exact(cuda, oracle):
+    """Quotients a few ulps from half-integers under arbitrary scales: the product with
+    the reciprocal scale must round like the IEEE quotient (the kernels fall back to the
+    division near a half-integer)."""
+    gen = torch.Generator().manual_seed(23)
+    T, H, D, P, ps = 64, 4, 128, 8, 16
+    x = _near_tie_rows(gen, T, H, D)
+    xv = _near_tie_rows(gen, T, H, D)
+    kp = torch.zeros(P, H, ps, D, dtype=torch.int8, device="cuda")
+    vp = torch.zeros_like(kp)
+    ks = torch.ones(P, H, ps, 1, dtype=torch.float32, device="cuda")
+    vs = torch.ones_like(ks)
+    slots = torch.randperm(P * ps, generator=gen)[:T]
+    write_slots(x.cuda(), xv.cuda(), slots.cuda(), kp, vp, ks, vs)
+    for src, pages, scales in ((x, kp, ks), (xv, vp, vs)):
+        q_ref, s_ref = oracle.quantize_int8_ref(to_np(src), 0)
+        pg, sc = to_np(pages), to_np(scales)
+        for t in range(T):
+            sl = int(slots[t])
+            np.testing.assert_array_equal(pg[sl // ps, :, sl % ps], q_ref[t])
+            np.testing.assert_array_equal(sc[sl // ps, :, sl % ps], s_ref[t])
+
+
 def test_paged_cache_matches_full_cache(cuda):
     gen = torch.Generator().manual_seed(3)
     pool = TinyKvPagedPool(page_size=4)

@@ -1214,7 +1214,19 @@ MmaPlan plan_paged_mma(const PagedArgs& a) {
     // (2 warps x 4 stages) let the most of them share an SM (one CTA per unit with a
     // producer and 12 consumer warps measured 1.9x slower on config 1: a unit's pages
     // have to come through many SMs)
-    const int dflt = plan.nwm == 0 ? kDefaultN8Variant : kDefaultDecodeVariant;
+    int dflt = plan.nwm == 0 ? kDefaultN8Variant : kDefaultDecodeVariant;
+    // n8 tile, 16-bit pages, short contexts, more units than the default variant's CTA
+    // slots but no more than those of 2 warps x 2 stages (8 CTAs per SM against 6): the
+    // smaller ring runs the launch as one wave (B = 128 at 1-1.1K keys, 32/8 heads: 92 us
+    // against 112 us).  Launches that need several waves either way keep the deeper ring
+    // (B = 160 at 600-1000 keys, 16/8 heads: 101 us against 107 us with 2 x 2; config 3:
+    // 2 x 4 stages 7249-7292 GB/s against 7090-7137).
+    if (plan.nwm == 0 && kv16 && !dense && env_int("NVM_ATTN_WAVE_RULE", 1) != 0) {
+      const int64_t units = a.B * a.Hkv, sms = sm_count_cached();
+      const int64_t tiles = (a.max_pages * a.page_size + 15) / 16;
+      if (tiles <= kOneWaveTiles && units > sms * n8_resident_per_sm(a, dflt) && units <= sms * n8_resident_per_sm(a, 2))
+        dflt = 2;
+    }
     plan.variant = (int)env_int("NVM_ATTN_DECODE_CFG", dflt);
     if (plan.variant < 0 || plan.variant > 8 || plan.variant == 5) plan.variant = 3;
     plan.nwk = kWarps1[plan.variant];

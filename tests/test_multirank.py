@@ -1,6 +1,6 @@
 """KV-head sharding across ranks (the N>1 path of bench.py) on CPU with gloo.
 
-Two gloo ranks each compute their shard of a paged decode with the oracle, gather
+Two, four and eight gloo ranks each compute their shard of a paged decode with the oracle, gather
 the shards on rank 0, and the stitched result must equal the unsharded oracle
 output bit for bit (attention is independent per kv head, so no collective is on
 the data path; the gather here is only the check).
@@ -66,16 +66,16 @@ def _worker(rank, world, port, result_path):
 
 @pytest.mark.parametrize("world", [2, 4, 8])
 def test_sharded_decode_equals_unsharded(oracle, tmp_path, world):
-    if world > 2:
-        # more ranks than fit comfortably on CPU: check the shard arithmetic only
-        q, kp, vp, bt, cl, ps = _problem()
-        B, Hq = q.shape[:2]
-        cover = np.zeros((B, Hq), dtype=int)
-        for r in range(world):
-            sh = kv_head_shard(r, world, Hq, kp.shape[1], B)
-            cover[sh.b_lo:sh.b_hi, sh.q_lo:sh.q_hi] += 1
-        assert (cover == 1).all()
-        return
+    # every (sequence, q head) is owned by exactly one rank (at 8 ranks the 4 kv heads
+    # are also split by batch halves) ...
+    q, kp, vp, bt, cl, ps = _problem()
+    B, Hq = q.shape[:2]
+    cover = np.zeros((B, Hq), dtype=int)
+    for r in range(world):
+        sh = kv_head_shard(r, world, Hq, kp.shape[1], B)
+        cover[sh.b_lo:sh.b_hi, sh.q_lo:sh.q_hi] += 1
+    assert (cover == 1).all()
+    # ... and the stitched shards computed by `world` gloo ranks equal the unsharded result
     path = str(tmp_path / "out.npy")
     mp.start_processes(_worker, args=(world, _free_port(), path), nprocs=world, join=True, start_method="spawn")
     q, kp, vp, bt, cl, ps = _problem()

@@ -656,6 +656,58 @@ def decode_line(name: str, peaks: dict, device, flush, cpu: bool, cpu_seconds: f
     return line
 
 
+def short_decode_results(peaks: dict, device, flush, batches=(64, 128)) -> list[dict]:
+    """Secondary lines: paged decode at a serving decode step's shape (Qwen3-4B heads
+    32 / 8, d 128, bf16, page 16, contexts U[1024, 1100], no shared pages), B = 64 and
+    128: one launch after an L2 flush like every other line, and the same launch back to
+    back in a CUDA graph over enough copies of the pools (different pages, > 1 GB in all)
+    that L2 holds none of them -- how a decode step's layers run, without the harness's
+    per-launch floor.  Parity: the single launch against the oracle on sampled rows."""
+    res = []
+    for B in batches:
+        cfg = dict(B=B, Hq=32, Hkv=8, L=1, D=128, ps=16, dtype=torch.bfloat16, ctx=("uniform", 1024, 1100),
+                   share=None, model="Qwen3-4B")
+        w = build_decode(cfg, 0, 1, device)
+        nbytes = w["bytes"]["total"]
+        times, out = time_launches(lambda: run_decode_step(w), 20, 3, flush)
+        ms = statistics.median(times)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        parity = parity_paged(w, out, sample_rows(cfg, B, 0, seed=13))
+        ncopy = max(4, int(1.2e9 // w["kp"].nbytes // 2) + 1)
+        copies = [w] + [build_decode(cfg, 0, 1, device, seed=s) for s in range(1, ncopy)]
+        outs = [torch.empty_like(out) for _ in copies]
+        for c, o in zip(copies, outs):
+            run_decode_step(c, out=o)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for c, o in zip(copies, outs):
+                run_decode_step(c, out=o)
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 10
+        e0.record()
+        for _ in range(reps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        g_us = e0.elapsed_time(e1) * 1000 / (reps * len(copies))
+        g_bytes = sum(c["bytes"]["total"] for c in copies) / len(copies)
+        g_gbs = g_bytes / (g_us * 1e-6) / 1e9
+        res.append(dict(workload=f"decode at the decode-step shape Qwen3-4B, B={B}, ctx U[1024,1100], bf16",
+                        metric="decode-attn KV GB/s", value=round(gbs, 1), unit="GB/s", ms=round(ms, 4),
+                        bytes=nbytes, spread=spread(times, nbytes, 1e9), roofline_frac=round(gbs / peaks["hbm"], 4),
+                        l2="flushed", graph_us_per_launch=round(g_us, 2), graph_gbs=round(g_gbs, 1),
+                        graph_roofline_frac=round(g_gbs / peaks["hbm"], 4),
+                        graph=f"{len(copies)} launches over distinct pools back to back, {reps} replays",
+                        parity=parity))
+        del graph, copies, outs, w, out
+        torch.cuda.empty_cache()
+    return res
+
+
 def secondary_results(peaks: dict, device, cpu: bool, cpu_seconds: float) -> list[dict]:
     from nano_vllm_b200 import flash_attention
 
@@ -663,6 +715,7 @@ def secondary_results(peaks: dict, device, cpu: bool, cpu_seconds: float) -> lis
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
     for name in ["c1", "c4", "c5"]:
         res.append(decode_line(name, peaks, device, flush, cpu, cpu_seconds))
+    res.extend(short_decode_results(peaks, device, flush))
     # 2a: dense causal prefill, 4 x 2048, 32/8 heads, bf16
     gen = torch.Generator(device=device)
     gen.manual_seed(5)
@@ -1061,6 +1114,21 @@ def run_qkprep(args):
     print(json.dumps(_single_line(r, args, peaks, "hbm", {"device_error_word": nv.device_error(device)})), flush=True)
 
 
+def run_shortdec(args):
+    """Paged decode at the decode-step shape (B = 64 and 128, or --batch), single launch
+    and back to back in a CUDA graph; one JSON line per batch."""
+    from nano_vllm_b200 import _native as nv
+
+    device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(device)
+    peaks = measured_peaks()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    for r in short_decode_results(peaks, device, flush, batches=(args.batch,) if args.batch else (64, 128)):
+        extra = {k: r[k] for k in ("graph_us_per_launch", "graph_gbs", "graph_roofline_frac", "graph")}
+        extra["device_error_word"] = nv.device_error(device)
+        print(json.dumps(_single_line(r, args, peaks, "hbm", extra)), flush=True)
+
+
 def run_w4a16(args):
     """The W4A16 matmul alone at Qwen3-4B's gate+up projection shape (M = --batch or 1
     activation rows); one JSON line."""
@@ -1150,6 +1218,8 @@ def run_ours(args):
         return run_qkprep(args)
     if args.config == "w4a16":
         return run_w4a16(args)
+    if args.config == "shortdec":
+        return run_shortdec(args)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -1341,7 +1411,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["c1", "c2a", "c2b", "c3", "c4", "c5", "qkprep", "w4a16", "step"],
+    ap.add_argument("--config", choices=["c1", "c2a", "c2b", "c3", "c4", "c5", "qkprep", "w4a16", "step", "shortdec"],
                     default="c3")
     ap.add_argument("--prior", type=int, default=0, help="config 2b: paged tokens before the 512-token chunk")
     ap.add_argument("--batch", type=int, default=None, help="override the config's batch (small profiling cases)")

@@ -1033,6 +1033,7 @@ int n8_resident_variant(int variant) {
     case 1: return n8_resident<KvT, ScaleT, D, 4, 12>();
     case 2: return n8_resident<KvT, ScaleT, D, 2, 2>();
     case 4: return n8_resident<KvT, ScaleT, D, 2, 8>();
+    case 5: return n8_resident<KvT, ScaleT, D, 4, 4>();
     case 6: return n8_resident<KvT, ScaleT, D, 1, 4>();
     case 7: return n8_resident<KvT, ScaleT, D, 2, 4>();
     case 8: return n8_resident<KvT, ScaleT, D, 1, 6>();
@@ -1154,6 +1155,7 @@ int launch_decode(const PagedArgs& a, const MmaPlan& plan, void* ws, cudaStream_
     case 2: return launch_cfg<KvT, ScaleT, D, NWM, 2, 2>(a, plan, ws, s);
     case 3: return launch_cfg<KvT, ScaleT, D, NWM, 2, 6>(a, plan, ws, s);
     case 4: return launch_cfg<KvT, ScaleT, D, NWM, 2, 8>(a, plan, ws, s);
+    case 5: return launch_cfg<KvT, ScaleT, D, NWM, 4, 4>(a, plan, ws, s);
     case 6: return launch_cfg<KvT, ScaleT, D, NWM, 1, 4>(a, plan, ws, s);
     case 7: return launch_cfg<KvT, ScaleT, D, NWM, 2, 4>(a, plan, ws, s);
     case 8: return launch_cfg<KvT, ScaleT, D, NWM, 1, 6>(a, plan, ws, s);
@@ -1209,7 +1211,7 @@ MmaPlan plan_paged_mma(const PagedArgs& a) {
   // variant -> consumer warps along keys (must match launch_decode / launch_m3)
   plan.variant = -1;
   if (plan.nwm <= 1) {
-    static const int kWarps1[9] = {4, 4, 2, 2, 2, 2, 1, 2, 1};
+    static const int kWarps1[9] = {4, 4, 2, 2, 2, 4, 1, 2, 1};
     // the n8 tile runs without a producer warp: small CTAs with a short ring
     // (2 warps x 4 stages) let the most of them share an SM (one CTA per unit with a
     // producer and 12 consumer warps measured 1.9x slower on config 1: a unit's pages
@@ -1228,7 +1230,7 @@ MmaPlan plan_paged_mma(const PagedArgs& a) {
         dflt = 2;
     }
     plan.variant = (int)env_int("NVM_ATTN_DECODE_CFG", dflt);
-    if (plan.variant < 0 || plan.variant > 8 || plan.variant == 5) plan.variant = 3;
+    if (plan.variant < 0 || plan.variant > 8) plan.variant = 3;
     plan.nwk = kWarps1[plan.variant];
   } else if (plan.nwm == 3) {
     static const int kWarps3[4] = {2, 1, 1, 2};

@@ -278,11 +278,12 @@ def test_validation_errors(cuda):
         paged_attention(q[:, :2], kp, kp.float(), bt, cl, 16)
 
 
-@pytest.mark.parametrize("variant", ["2", "7", "3", "4"], ids=["ring2", "ring4", "ring6", "ring8"])
+@pytest.mark.parametrize("variant", ["2", "7", "3", "4", "5"], ids=["ring2", "ring4", "ring6", "ring8", "w4ring4"])
 @pytest.mark.parametrize("kvd", [torch.bfloat16, torch.int8])
 def test_n8_ring_depths_match_oracle(cuda, oracle, kvd, variant, monkeypatch):
-    """The n8 decode tile (no producer warp: each of its 2 warps refills the ring stages
-    it consumes) at every 2-warp ring depth that NVM_ATTN_DECODE_CFG can select, on
+    """The n8 decode tile (no producer warp: each warp refills the ring stages it
+    consumes) at every 2-warp ring depth that NVM_ATTN_DECODE_CFG can select and with 4
+    warps of one stage each, on
     ragged split-K contexts with page holes and a row count that leaves the tile part empty."""
     monkeypatch.setenv("NVM_ATTN_DECODE_CFG", variant)
     monkeypatch.setenv("NVM_ATTN_CHUNK_TILES", "16")

@@ -93,6 +93,7 @@ struct Sm100Params {
   const int* item_list;   // items with work, largest first (plan kernel); null: every item index
   const int* item_count;  // length of item_list
   int stage_out;      // one item per CTA: O leaves through shared memory and bulk tensor stores
+  int pv_wait;        // 1: S_{j+2} waits for PV_j to complete (see the MMA issuer)
   int* exit_counter;  // CTAs done; the last one resets both counters
   int* counters;
   float2* part_ml;  // [n_units][n_chunks][rows_real]
@@ -119,23 +120,32 @@ __device__ __forceinline__ Item decode_item(const Sm100Params& p, int64_t item) 
   // Chunk-major, last chunk first: a chunk c >= 1 exists only for long units and is then
   // full-size (except each unit's last), so handing out high chunks first and the mixed
   // chunk-0 items (short units included) last approximates longest-first scheduling.
-  it.c = p.n_chunks - 1 - item / p.n_units;
-  it.u = item % p.n_units;
+  // The divisions run on 32-bit values (the plan bounds items, rows and tiles below
+  // 2^31): 64-bit divisions here cost about a microsecond on the producer's path to
+  // its first copy.
+  const uint32_t item32 = (uint32_t)item, nu = (uint32_t)p.n_units, no = (uint32_t)p.n_outer;
+  const uint32_t cq = item32 / nu, u32 = item32 - cq * nu;
+  it.c = p.n_chunks - 1 - (int64_t)cq;
+  it.u = u32;
   // Row-tile-major, heavy (late, causal) row tiles first across all heads: dispatch in
   // item order is then longest-first.
-  const int64_t rt = p.n_row_tiles - 1 - it.u / p.n_outer;
-  it.n = it.u % p.n_outer;  // flat (b, q head), or (b, kv head) when grouped
-  it.b = p.grouped ? it.n / p.Hkv : it.n / p.Hq;
-  it.kvh = p.grouped ? it.n % p.Hkv : (it.n % p.Hq) / p.g;
+  const uint32_t rq = u32 / no, n32 = u32 - rq * no;
+  const int64_t rt = p.n_row_tiles - 1 - (int64_t)rq;
+  it.n = n32;  // flat (b, q head), or (b, kv head) when grouped
+  const uint32_t hd = (uint32_t)(p.grouped ? p.Hkv : p.Hq);
+  const uint32_t b32 = n32 / hd, h32 = n32 - b32 * hd;
+  it.b = b32;
+  it.kvh = p.grouped ? h32 : h32 / (uint32_t)p.g;
   it.ctx = p.dense ? p.dense_ctx : (int64_t)p.context_lens[it.b];
   const int64_t cap = p.mp * p.ps;
   it.ctx_limit = it.ctx < cap ? it.ctx : cap;
   it.r0 = rt * kBM;  // first row of the tile inside the unit
   it.rows = (p.M_rows - it.r0) < kBM ? (p.M_rows - it.r0) : kBM;
   // query positions l = r % L of the tile's rows: the smallest and the largest
-  const bool wraps = it.rows >= p.L || (it.r0 % p.L) + it.rows > p.L;
-  it.l_first = wraps ? 0 : it.r0 % p.L;
-  const int64_t l_last = wraps ? p.L - 1 : (it.r0 + it.rows - 1) % p.L;
+  const int64_t r0_mod = (int64_t)((uint32_t)it.r0 % (uint32_t)p.L);
+  const bool wraps = it.rows >= p.L || r0_mod + it.rows > p.L;
+  it.l_first = wraps ? 0 : r0_mod;
+  const int64_t l_last = wraps ? p.L - 1 : (int64_t)((uint32_t)(it.r0 + it.rows - 1) % (uint32_t)p.L);
   int64_t need = it.ctx_limit;
   if (p.causal) {
     const int64_t lim = l_last + it.ctx - p.L + 1;
@@ -143,7 +153,7 @@ __device__ __forceinline__ Item decode_item(const Sm100Params& p, int64_t item) 
   }
   if (it.ctx <= 0 || need < 0) need = 0;
   const int64_t n_tiles_unit = (need + kBN - 1) / kBN;
-  it.n_chunks_unit = n_tiles_unit > 0 ? (n_tiles_unit + p.ct - 1) / p.ct : 1;
+  it.n_chunks_unit = n_tiles_unit > 0 ? (int64_t)((uint32_t)(n_tiles_unit + p.ct - 1) / (uint32_t)p.ct) : 1;
   it.valid = it.c < it.n_chunks_unit;
   it.t_begin = it.c * p.ct;
   const int64_t left = n_tiles_unit - it.t_begin;
@@ -178,7 +188,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint64_t* v_empty = v_full + kVStages;     // [kVStages] PV has read it
   uint64_t* s_full = v_empty + kVStages;     // [2] S_G in TMEM buffer G&1
   uint64_t* p_full = s_full + 2;             // [2] P_G written over S_G (count 128)
-  uint64_t* o_done = p_full + 2;             // PV_G complete (one completion per tile)
+  uint64_t* o_done = p_full + 2;             // PV_G complete (only with pv_wait)
   uint64_t* item_done = o_done + 1;          // every PV of an item complete (one per item)
   uint64_t* o_free = item_done + 1;          // the softmax warps have read an item's O (count 128)
   uint64_t* mma_done = o_free + 1;           // every MMA of the CTA complete (teardown)
@@ -190,7 +200,11 @@ __global__ void __launch_bounds__(kThreads, 2)
   int64_t* item_ring = reinterpret_cast<int64_t*>(reinterpret_cast<uint8_t*>(bars) + 256);  // [4]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (threadIdx.x == 0) {
+  // The producer warp's first lane sets up the barriers; with one item per CTA it then
+  // requests that item's Q tile at once, before tensor memory is allocated and the CTA
+  // synchronises (the first S waits on this copy).
+  int q_early = 0;
+  if (threadIdx.x == 4 * 32) {
     mbar_init(q_full, 1);
     mbar_init(q_empty, 1);
     for (int s = 0; s < kKStages; ++s) {
@@ -215,6 +229,15 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     *abort_flag = 0;
     fence_mbar_init();
+    if (p.stage_out && (int64_t)blockIdx.x < p.n_items) {
+      const Item it0 = decode_item(p, blockIdx.x);
+      if (it0.valid && it0.n_tiles > 0) {
+        mbar_arrive_expect_tx(q_full, kQBytes);
+        tma_load_3d(sQ, &tm_q, 0, (int)it0.r0, (int)it0.n, q_full);
+        tma_load_3d(sQ + kBM * 128, &tm_q, 64, (int)it0.r0, (int)it0.n, q_full);
+        q_early = 1;
+      }
+    }
   }
   if (warp == 5) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
@@ -248,6 +271,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     // The whole warp runs the loop and one elected lane issues the copies.  Per item:
     // publish the item index, load Q (once the previous item's last S has read sQ), then
     // K_0, K_1, V_0, K_2, V_1, ... into the rings.
+    q_early = __shfl_sync(0xffffffffu, q_early, 0);  // the first item's Q is already on its way
     const bool leader = elect_one();
     const int leader_lane = __ffs(__ballot_sync(0xffffffffu, leader)) - 1;
     int gk = 0, gv = 0;  // K / V tiles issued by this CTA so far
@@ -302,7 +326,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         ok = false;
         break;
       }
-      if (leader) {
+      if (leader && !(iw == 0 && q_early)) {
         mbar_arrive_expect_tx(q_full, kQBytes);
         tma_load_3d(sQ, &tm_q, 0, (int)it.r0, (int)it.n, q_full);
         tma_load_3d(sQ + kBM * 128, &tm_q, 64, (int)it.r0, (int)it.n, q_full);
@@ -401,8 +425,9 @@ __global__ void __launch_bounds__(kThreads, 2)
     __syncwarp();
   } else if (warp == 5) {
     // ---------------------------------------------------------------- MMA issuer
-    // The whole warp waits and loops; one elected lane issues the MMAs and the commits
-    // (a commit tracks the MMAs of the thread that issues it, so it is always the same lane).
+    // The whole warp waits and loops; the MMAs and commits are issued through the
+    // whole-warp forms, whose elect.sync picks the same lane every time (a commit tracks
+    // the MMAs of the thread that issues it).
     const bool leader = elect_one();
     const uint32_t id_qk = idesc<T>(false, kBN);
     const uint32_t id_pv = idesc<T>(true, kD);
@@ -432,14 +457,11 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks) db[ks] = dks + (uint64_t)((((ks >> 2) * (kBN * 128)) + (ks & 3) * 32) >> 4);
       const uint32_t td = tmem + (uint32_t)((gs & 1) * kBN);
-      if (leader) {
 #pragma unroll
-        for (int ks = 0; ks < kD / 16; ++ks) mma_f16(td, dq[ks], db[ks], id_qk, ks > 0 ? 1u : 0u);
-        mma_commit(&s_full[gs & 1]);
-        mma_commit(&k_empty[s]);
-        if (last_of_item) mma_commit(q_empty);
-      }
-      __syncwarp();
+      for (int ks = 0; ks < kD / 16; ++ks) mma_f16_warp(td, dq[ks], db[ks], id_qk, ks > 0 ? 1u : 0u);
+      mma_commit_warp(&s_full[gs & 1]);
+      mma_commit_warp(&k_empty[s]);
+      if (last_of_item) mma_commit_warp(q_empty);
       ++gs;
     };
     while (ok) {
@@ -492,22 +514,22 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks) db[ks] = dvs + (uint64_t)((ks * 16 * 128) >> 4);
         const uint32_t tp = tmem + (uint32_t)((gp & 1) * kBN);
-        if (leader) {
 #pragma unroll
-          for (int ks = 0; ks < kBN / 16; ++ks) {
-            mma_f16_ts(tO, tp + (uint32_t)(ks * 8), db[ks], id_pv, (j > 0 || ks > 0) ? 1u : 0u);
-            if (split) mma_f16_ts(tO, tp + (uint32_t)(kBN / 2 + ks * 8), db[ks], id_pv, 1u);
-          }
-          mma_commit(o_done);
-          mma_commit(&v_empty[vs]);
-          if (j == n - 1) mma_commit(item_done);
+        for (int ks = 0; ks < kBN / 16; ++ks) {
+          mma_f16_ts_warp(tO, tp + (uint32_t)(ks * 8), db[ks], id_pv, (j > 0 || ks > 0) ? 1u : 0u);
+          if (split) mma_f16_ts_warp(tO, tp + (uint32_t)(kBN / 2 + ks * 8), db[ks], id_pv, 1u);
         }
-        __syncwarp();
+        if (p.pv_wait) mma_commit_warp(o_done);
+        mma_commit_warp(&v_empty[vs]);  // also tells the softmax warps that PV_j is complete
+        if (j == n - 1) mma_commit_warp(item_done);
         const int gj = gp++;
-        // S_{j+2} reuses S_j's TMEM columns, which hold P_j: wait until PV_j has
-        // finished reading them (o_done phase of PV_j) before overwriting.
+        // S_{j+2} reuses S_j's TMEM columns, which hold P_j, the A operand of PV_j.  It is
+        // issued right behind PV_j by the same thread: this thread's tcgen05.mma
+        // operations execute in issue order, so PV_j has read P_j before S_{j+2} writes
+        // there (results bit-identical with an explicit completion wait, which
+        // NVM_SM100_PV_WAIT=1 restores; not waiting measured 4-12 % faster on prefill).
         if (j + 2 < n) {
-          if (!wait_k() || !warp_wait(o_done, (uint32_t)(gj & 1))) {
+          if (!wait_k() || (p.pv_wait && !warp_wait(o_done, (uint32_t)(gj & 1)))) {
             ok = false;
             break;
           }
@@ -516,20 +538,19 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       ++iw;
     }
-    if (leader) {
-      if (!ok) {
-        record_error(p.err, kDevErrMmaWait);
-        *(volatile int*)abort_flag = 1;
-      }
-      mma_commit(mma_done);
+    if (leader && !ok) {
+      record_error(p.err, kDevErrMmaWait);
+      *(volatile int*)abort_flag = 1;
     }
     __syncwarp();
+    mma_commit_warp(mma_done);
   } else {
     // ---------------------------------------------------------------- softmax warps 0-3
     const int row = warp * 32 + lane;            // TMEM lane == query row in the tile
     const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
     const float sl2 = p.scale_log2;              // > 0, so max(s) * sl2 == max(s * sl2)
     const int esz = p.out_dtype == NVM_F32 ? 4 : 2;
+    const bool staged = p.stage_out != 0;  // O through shared memory and bulk tensor stores
     int gt = 0;  // tiles processed by this CTA so far
     int kq = 0, iw = 0;
     bool ok = true;
@@ -676,16 +697,17 @@ __global__ void __launch_bounds__(kThreads, 2)
             }
           }
         }
-        // row max as a tree (8 independent chains), not one 64-long dependency chain
+        // row max as a tree of three-input maxima (8 independent chains of 8 scores, then
+        // the 8 chain results): 36 instructions instead of 63
         float mv[8];
 #pragma unroll
-        for (int x = 0; x < 8; ++x) mv[x] = sv[x];
-#pragma unroll
-        for (int c = 8; c < kBN; c += 8) {
-#pragma unroll
-          for (int x = 0; x < 8; ++x) mv[x] = fmaxf(mv[x], sv[c + x]);
+        for (int x = 0; x < 8; ++x) {
+          float t = fmax3(sv[x], sv[8 + x], sv[16 + x]);
+          t = fmax3(t, sv[24 + x], sv[32 + x]);
+          t = fmax3(t, sv[40 + x], sv[48 + x]);
+          mv[x] = fmaxf(t, sv[56 + x]);
         }
-        const float mx = fmaxf(fmaxf(fmaxf(mv[0], mv[1]), fmaxf(mv[2], mv[3])), fmaxf(fmaxf(mv[4], mv[5]), fmaxf(mv[6], mv[7])));
+        const float mx = fmax3(fmax3(mv[0], mv[1], mv[2]), fmax3(mv[3], mv[4], mv[5]), fmaxf(mv[6], mv[7]));
         const float mx_s = mx * sl2;
         // lazy max: keep the old reference max unless the new one exceeds it by > 8
         float m_ref = m;
@@ -730,7 +752,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         m = m_ref;
         if (__any_sync(0xffffffffu, rescale)) {
           // O must hold PV_{j-1} before it is rescaled
-          if (!warp_wait(o_done, (uint32_t)((g - 1) & 1))) {
+          if (!warp_wait(&v_empty[(g - 1) % kVStages], (uint32_t)(((g - 1) / kVStages) & 1))) {
             ok = false;
             break;
           }
@@ -789,7 +811,7 @@ __global__ void __launch_bounds__(kThreads, 2)
             tc_fence_before();
             mbar_arrive(o_free);
           }
-          if (p.stage_out) {
+          if (staged) {
             stage32(ov2, c1, inv);
             stage32(ov2 + 32, c1 + 32, inv);
           } else if (row_ok) {
@@ -797,7 +819,7 @@ __global__ void __launch_bounds__(kThreads, 2)
             store32(orow, ov2 + 32, c1 + 32, inv);
           }
         }
-        if (p.stage_out) flush_staged(it);
+        if (staged) flush_staged(it);
       } else {
         // Split-K: leave this chunk's (m, l) and unnormalised O rows in the workspace ...
         const int64_t prow = (it.u * p.n_chunks + it.c) * p.rows_real + row;
@@ -906,11 +928,11 @@ __global__ void __launch_bounds__(kThreads, 2)
                   }
                 }
               }
-              if (p.stage_out) stage32(acc2, c0, inv);
+              if (staged) stage32(acc2, c0, inv);
               else store32(orow, acc2, c0, inv);
             }
           }
-          if (p.stage_out) flush_staged(it);
+          if (staged) flush_staged(it);
           if (row == 0) p.counters[it.u] = 0;  // tickets start at zero for the next call
         }
       }
@@ -1050,11 +1072,13 @@ Sm100Plan plan_sm100(const PagedArgs& a, bool sizing_only) {
   } else {
     return plan;
   }
+  if (plan.M_rows >= INT32_MAX) return plan;  // the item decode divides in 32 bits
   plan.n_row_tiles = (plan.M_rows + kBM - 1) / kBM;
   plan.n_units = plan.n_outer * plan.n_row_tiles;
   plan.rows_real = plan.M_rows < kBM ? plan.M_rows : kBM;
   const int64_t keys = a.dense ? a.page_size : a.max_pages * a.page_size;
   const int64_t tiles_max = (keys + kBN - 1) / kBN;
+  if (tiles_max >= INT32_MAX / 2) return plan;
   plan.ct = tiles_max > 0 ? tiles_max : 1;
   plan.n_chunks = 1;
   // Split-K over keys for grouped paged calls (dense callers pass no workspace): aim at
@@ -1152,6 +1176,7 @@ int launch_sm100(const PagedArgs& a, const Sm100Plan& plan, void* ws, cudaStream
     if (ctas > 2 * (int64_t)sms) ctas = 2 * (int64_t)sms;
   }
   p.stage_out = ctas == p.n_items ? 1 : 0;
+  p.pv_wait = env_int("NVM_SM100_PV_WAIT", 1) != 0 ? 1 : 0;
   if (p.stage_out) p.work_counter = p.exit_counter = nullptr;  // one item per CTA: item = blockIdx.x
   if (p.work_counter != nullptr && env_int("NVM_SM100_PLAN", 1) != 0) {
     int* list = reinterpret_cast<int*>(static_cast<uint8_t*>(ws) + wo.list);

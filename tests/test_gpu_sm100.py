@@ -104,3 +104,27 @@ def test_dense_negative_scale(cuda, oracle):
     ref = oracle.flash_attention_ref(q.float().numpy(), k.float().numpy(), v.float().numpy(), scale=-0.05,
                                      mask="causal", nthreads=8)
     assert_close(out, ref, TOL16)
+
+
+@pytest.mark.parametrize("kind", ["dense", "chunked", "grouped"])
+def test_pv_issue_order_bit_identical(cuda, monkeypatch, kind):
+    """S_{j+2} issued right behind PV_j (NVM_SM100_PV_WAIT=0, relying on in-order
+    execution of one thread's tcgen05.mma) gives the same bits as the default, which
+    waits for PV_j to complete before S_{j+2} overwrites P_j."""
+    gen = torch.Generator().manual_seed(17)
+    if kind == "dense":
+        q = torch.randn(2, 8, 1024, 128, generator=gen).bfloat16().cuda()
+        k = torch.randn(2, 2, 1024, 128, generator=gen).bfloat16().cuda()
+        v = torch.randn(2, 2, 1024, 128, generator=gen).bfloat16().cuda()
+        run = lambda: flash_attention(q, k, v, mask="causal")  # noqa: E731
+    else:
+        L = 384 if kind == "chunked" else 5
+        prob = random_paged_problem(gen, 4, 16, 4, L, 128, 16, torch.bfloat16, 600, 3000)
+        run = lambda: paged_attention(prob["q"], prob["kp"], prob["vp"], prob["bt"], prob["cl"], 16,  # noqa: E731
+                                      mask="causal")
+    monkeypatch.setenv("NVM_SM100_PV_WAIT", "1")
+    a = run()
+    monkeypatch.setenv("NVM_SM100_PV_WAIT", "0")
+    b = run()
+    assert torch.equal(a, b)
+    assert nv.device_error(cuda) == 0

@@ -523,11 +523,11 @@ __global__ void __launch_bounds__(kThreads, 2)
         mma_commit_warp(&v_empty[vs]);  // also tells the softmax warps that PV_j is complete
         if (j == n - 1) mma_commit_warp(item_done);
         const int gj = gp++;
-        // S_{j+2} reuses S_j's TMEM columns, which hold P_j, the A operand of PV_j.  It is
-        // issued right behind PV_j by the same thread: this thread's tcgen05.mma
-        // operations execute in issue order, so PV_j has read P_j before S_{j+2} writes
-        // there (results bit-identical with an explicit completion wait, which
-        // NVM_SM100_PV_WAIT=1 restores; not waiting measured 4-12 % faster on prefill).
+        // S_{j+2} reuses S_j's TMEM columns, which hold P_j, the A operand of PV_j, so by
+        // default it waits until PV_j has completed.  NVM_SM100_PV_WAIT=0 issues it right
+        // behind PV_j instead, relying on one thread's MMAs executing in issue order: about
+        // 1 % faster on prefill and bit-identical in every test, but no documented rule we
+        // could confirm covers a later MMA overwriting an earlier one's A operand.
         if (j + 2 < n) {
           if (!wait_k() || (p.pv_wait && !warp_wait(o_done, (uint32_t)(gj & 1)))) {
             ok = false;

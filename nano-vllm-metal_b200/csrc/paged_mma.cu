@@ -153,10 +153,17 @@ __global__ void __launch_bounds__(Cfg<KvT, D, NWM, NWK, NS_>::kThreads)
   int* s_flag = tile_pid + kMaxChunkTiles;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // 32-bit index arithmetic (the plan bounds units, rows and tiles below 2^31): a 64-bit
+  // division costs about a hundred instructions, and these sit in front of the first
+  // page copies.
   const int64_t unit = blockIdx.x;
-  const int64_t rb = unit % p.n_rb;
-  const int64_t bh = unit / p.n_rb;
-  const int64_t h = bh % p.Hkv, b = bh / p.Hkv;
+  const uint32_t u32 = blockIdx.x, nrb = (uint32_t)p.n_rb, hkv = (uint32_t)p.Hkv;
+  const uint32_t bh32 = u32 / nrb;
+  const int64_t rb = u32 - bh32 * nrb;
+  const uint32_t b32 = bh32 / hkv;
+  const int64_t h = bh32 - b32 * hkv, b = b32;
+  // paged: 16-token tiles per page (page_size is a multiple of 16)
+  const uint32_t tpp = (uint32_t)(p.ps >> 4);
   const int64_t c = blockIdx.y;
 
   const int64_t ctx = p.context_lens ? (int64_t)p.context_lens[b] : p.dense_ctx;
@@ -249,7 +256,10 @@ __global__ void __launch_bounds__(Cfg<KvT, D, NWM, NWK, NS_>::kThreads)
     for (int j = 0; j < kPer; ++j) {
       const int i = lane + 32 * j;
       pv[j] = -1;
-      if (i < n_tab) pv[j] = p.block_table ? (int64_t)__ldg(&p.block_table[b * p.mp + ((t_begin + i) * 16) / p.ps]) : b;
+      if (i < n_tab) {
+        const uint32_t tile = (uint32_t)(t_begin + i);
+        pv[j] = p.block_table ? (int64_t)__ldg(&p.block_table[b * p.mp + (tpp == 1 ? tile : tile / tpp)]) : b;
+      }
     }
 #pragma unroll
     for (int j = 0; j < kPer; ++j) {
@@ -261,14 +271,14 @@ __global__ void __launch_bounds__(Cfg<KvT, D, NWM, NWK, NS_>::kThreads)
 
   int64_t need_keys = ctx_limit;
   if (p.causal) {
-    const bool spans = rows_here >= p.L || (row0 % p.L) + rows_here > p.L;
-    const int64_t lmax = spans ? p.L - 1 : (row0 + rows_here - 1) % p.L;
+    const bool spans = rows_here >= p.L || (int64_t)((uint32_t)row0 % (uint32_t)p.L) + rows_here > p.L;
+    const int64_t lmax = spans ? p.L - 1 : (int64_t)((uint32_t)(row0 + rows_here - 1) % (uint32_t)p.L);
     const int64_t lim = lmax + ctx - p.L + 1;
     if (lim < need_keys) need_keys = lim;
   }
   if (ctx <= 0 || need_keys < 0) need_keys = 0;
   const int64_t n_tiles = (need_keys + 15) / 16;
-  const int64_t n_chunks = n_tiles > 0 ? (n_tiles + p.ct - 1) / p.ct : 1;
+  const int64_t n_chunks = n_tiles > 0 ? (int64_t)((uint32_t)(n_tiles + p.ct - 1) / (uint32_t)p.ct) : 1;
   // A chunk past this unit's keys has nothing to do; inside a cluster it still takes
   // part in the cluster barriers of the merge (with no tiles), so it does not return.
   if (c >= n_chunks && !(C::kClusterFits && p.cluster)) return;
@@ -282,7 +292,8 @@ __global__ void __launch_bounds__(Cfg<KvT, D, NWM, NWK, NS_>::kThreads)
     const int pid = tile_pid[i];
     stage_valid[s] = pid >= 0 ? 1 : 0;
     if (pid >= 0) {
-      const int slot0 = (int)(((t_begin + i) * 16) % p.ps);
+      const uint32_t tile = (uint32_t)(t_begin + i);
+      const int slot0 = p.block_table ? (tpp == 1 ? 0 : (int)((tile % tpp) * 16)) : (int)(((t_begin + i) * 16) % p.ps);
       uint8_t* st = smem + s * C::kStageBytes;
       mbar_arrive_expect_tx(&full[s], 2 * C::kTileBytes + (C::kI8 ? 64 : 0));
 #pragma unroll
@@ -352,8 +363,8 @@ __global__ void __launch_bounds__(Cfg<KvT, D, NWM, NWK, NS_>::kThreads)
   const int64_t BIG = INT64_MAX / 4;
   int64_t limA = BIG, limB = BIG;
   if (p.causal) {
-    if (sA < p.M) limA = (sA % p.L) + ctx - p.L;
-    if (sB < p.M) limB = (sB % p.L) + ctx - p.L;
+    if (sA < p.M) limA = (int64_t)((uint32_t)sA % (uint32_t)p.L) + ctx - p.L;
+    if (sB < p.M) limB = (int64_t)((uint32_t)sB % (uint32_t)p.L) + ctx - p.L;
   }
   // Keys below `clean` are visible to every real row of this warp: no masking there.
   int64_t clean = ctx_limit;
@@ -903,7 +914,8 @@ __global__ void __launch_bounds__(Cfg<KvT, D, NWM, NWK, NS_>::kThreads)
     float* wlc = wm + n_chunks * rows_here;      // [n_chunks][rows_here]: l
     float* wl = wlc + n_chunks * rows_here;      // [rows_here]: sum of l * f
     for (int64_t i = tid; i < n_chunks * rows_here; i += NCT) {
-      const int64_t cc = i / rows_here, rl = i % rows_here;
+      const uint32_t cc32 = (uint32_t)i / (uint32_t)rows_here;
+      const int64_t cc = cc32, rl = (int64_t)((uint32_t)i - cc32 * (uint32_t)rows_here);
       const float2 ml = __ldcg(&p.part_ml[base + cc * p.rows_real + rl]);
       wm[i] = ml.x;
       wlc[i] = ml.y;
@@ -1247,6 +1259,8 @@ MmaPlan plan_paged_mma(const PagedArgs& a) {
   int64_t keys = a.max_pages * a.page_size;
   if (dense) keys = a.page_size;
   const int64_t tiles_max = (keys + 15) / 16;
+  // the kernel's index arithmetic runs in 32 bits
+  if (tiles_max >= INT32_MAX / 2 || M >= INT32_MAX) return plan;
   int64_t ct;
   if (dense || !can_split) {
     ct = tiles_max;  // dense callers pass no workspace: never split

@@ -53,10 +53,28 @@ __global__ void __launch_bounds__(kWarps * 32) kv_write_kernel(KvWriteParams p) 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t w = (int64_t)blockIdx.x * kWarps + warp;
   if (w >= p.T * p.Hkv) return;
-  const int64_t t = w / p.Hkv, h = w % p.Hkv;
+  // 32-bit divisions where the values fit (a 64-bit division costs about as much as
+  // copying the row)
+  int64_t t, h;
+  if (w <= 0x7fffffffLL && p.Hkv <= 0x7fffffffLL) {
+    const uint32_t tu = (uint32_t)w / (uint32_t)p.Hkv;
+    t = tu;
+    h = (uint32_t)w - tu * (uint32_t)p.Hkv;
+  } else {
+    t = w / p.Hkv;
+    h = w - t * p.Hkv;
+  }
   const int64_t slot = p.slots[t];
   if (slot < 0) return;
-  const int64_t pid = slot / p.ps, off = slot % p.ps;
+  int64_t pid, off;
+  if (slot <= 0x7fffffffLL && p.ps <= 0x7fffffffLL) {
+    const uint32_t pu = (uint32_t)slot / (uint32_t)p.ps;
+    pid = pu;
+    off = (uint32_t)slot - pu * (uint32_t)p.ps;
+  } else {
+    pid = slot / p.ps;
+    off = slot - pid * p.ps;
+  }
   if (pid >= p.P) return;  // out-of-pool slot: skipped (the host validates before launch)
   const int64_t row = (pid * p.Hkv + h) * p.ps + off;  // destination row index
   const int64_t src_off = t * p.st + h * p.sh;          // element offset of the source row

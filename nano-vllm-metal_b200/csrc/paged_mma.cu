@@ -1302,7 +1302,12 @@ MmaPlan plan_paged_mma(const PagedArgs& a) {
         }
       }
       if (!one_wave) {
-        const int64_t floor_ct = tiles_max < 48 ? tiles_max : 48;
+        int64_t floor_ct = tiles_max < 48 ? tiles_max : 48;
+        // Long contexts (>= 16K keys) with units enough for two waves of 128-tile chunks:
+        // chunks of at least 128 tiles (one rank's kv-head shard of config 3 at 8 GPUs,
+        // 256 units of 4K-32K keys: 380 us against 387 us with the six-wave 80 tiles;
+        // config 4's 160 and config 3's 256 are above the floor anyway).
+        if (tiles_max >= 1024 && plan.n_units * ((tiles_max + 127) / 128) >= 2 * slots) floor_ct = 128;
         if (ct < floor_ct) ct = floor_ct;
       }
     }

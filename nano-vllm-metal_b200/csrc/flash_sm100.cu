@@ -977,14 +977,34 @@ __global__ void __launch_bounds__(1024) sm100_plan_kernel(const Sm100Params p, i
     atomicAdd(&hist[bin], 1);
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int acc = 0;
-    for (int b = 0; b < kPlanBins; ++b) {
-      const int c = hist[b];
-      hist[b] = acc;
-      acc += c;
+  // Exclusive prefix sum of the bins, one bin per thread: a scan inside each warp, then
+  // over the 32 warp totals (a serial loop over the 1024 bins by one thread took ~10 us).
+  static_assert(kPlanBins == 1024, "one bin per thread of the 1024-thread plan CTA");
+  __shared__ int wsum[32];
+  {
+    const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
+    const int v = hist[threadIdx.x];
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
     }
-    *count = acc;
+    if (lane == 31) wsum[wp] = x;
+    __syncthreads();
+    if (wp == 0) {
+      int w = wsum[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, w, o);
+        if (lane >= o) w += y;
+      }
+      wsum[lane] = w;  // inclusive over warps
+    }
+    __syncthreads();
+    const int excl = x - v + (wp > 0 ? wsum[wp - 1] : 0);
+    hist[threadIdx.x] = excl;
+    if (threadIdx.x == kPlanBins - 1) *count = excl + v;
   }
   __syncthreads();
   for (int64_t item = threadIdx.x; item < p.n_items; item += blockDim.x) {

@@ -39,6 +39,18 @@ def test_decode_configs_at_bench_size(cuda, name):
     assert nv.device_error(cuda) == 0
 
 
+@pytest.mark.parametrize("world,rank", [(8, 0), (8, 7), (4, 1), (2, 0)])
+def test_config3_rank_shards(cuda, world, rank):
+    """One rank's kv-head shard of config 3 as the multi-GPU bench builds it (the planner
+    sizes its chunks from the shard's units, e.g. the 128-tile floor at 8 ranks)."""
+    cfg = bench.decode_config("c3")
+    w = bench.build_decode(cfg, rank, world, cuda)
+    out = bench.run_decode_step(w)
+    torch.cuda.synchronize()
+    _check(bench.parity_paged(w, out, bench.sample_rows(cfg, w["q"].shape[0], w["shard"].b_lo, seed=7)))
+    assert nv.device_error(cuda) == 0
+
+
 def test_dense_prefill_config2a_full_shape(cuda):
     gen = torch.Generator(device=cuda)
     gen.manual_seed(5)
